@@ -1,0 +1,392 @@
+"""Decode throughput of the B200 TP path: ``python bench.py --gpus N --steps K --warmup W``.
+
+One step = one fixed-length greedy generation over a batch of synthetic
+prompts (Qwen2.5-0.5B shape by default: B=1, prompt 128, 128 new tokens,
+bf16, seeded random weights) at TP = N (one process per GPU under torchrun).
+The prefill runs eagerly; the 127 decode steps are replays of one CUDA graph
+of the device-resident decode step.
+
+Reported (rank 0, one JSON line):
+* value: decode tokens/s = B * decode steps / decode time, where the decode
+  time is measured with CUDA events per step and the max over ranks is taken.
+* e2e: the same metric through ``generate_greedy``, starting from pinned host
+  prompt ids and ending with the output ids copied back to the host.
+* roofline: the dominant kernel (the LM-head GEMV streams the largest weight
+  of the token), timed live with CUDA events over repeated launches;
+  achieved = its weight bytes / launch time. roofline_token: (weight + KV)
+  bytes read per token per rank / measured time per token.
+* cpu_baseline: the CPU oracle port of the reference (rank 0, N=1 only) on
+  a bounded sample (prefill + 8 decode tokens).
+``--impl reference`` times that CPU port as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+MEASURED_PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--model", default="qwen2.5-0.5b", choices=["qwen2.5-0.5b", "qwen2.5-7b", "tiny"])
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt", type=int, default=None)
+    p.add_argument("--new-tokens", type=int, default=None)
+    p.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
+    p.add_argument("--gen-device", default=None, help="where synthetic weights are drawn (cpu|cuda)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-pdl", action="store_true")
+    p.add_argument("--out", default=None, help="also write the JSON line here")
+    return p.parse_args(argv)
+
+
+def workload(args):
+    from minitp_b200 import config as mcfg
+
+    if args.model == "qwen2.5-7b":
+        cfg, prompt, new = mcfg.qwen25_7b(), 1024, 256
+    elif args.model == "tiny":
+        cfg, prompt, new = mcfg.baseline_tiny(), 8, 16
+    else:
+        cfg, prompt, new = mcfg.qwen25_05b(), 128, 128
+    return cfg, args.prompt or prompt, args.new_tokens or new
+
+
+def peaks():
+    try:
+        with open(MEASURED_PEAKS) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------- #
+# clocks
+# ---------------------------------------------------------------------- #
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="mtpb_clocks_", suffix=".csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.idx)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------- #
+# bytes per token
+# ---------------------------------------------------------------------- #
+def weight_bytes_per_token(model) -> int:
+    """Weight bytes one decode step streams on this rank (all GEMV weights + LM head)."""
+    n = model.lm_head.weight.numel()
+    for layer in model.model.layers:
+        a, m = layer.self_attn, layer.mlp
+        n += a.qkv_proj.weight.numel() + a.o_proj.weight.numel()
+        n += m.gate_up_proj.weight.numel() + m.down_proj.weight.numel()
+    return n * model.lm_head.weight.element_size()
+
+
+def kv_bytes_per_token(model, batch: int, avg_len: float) -> float:
+    a = model.model.layers[0].self_attn
+    per_pos = 2 * a.kv_heads_local * a.head_dim * model.lm_head.weight.element_size()
+    return per_pos * avg_len * batch * len(model.model.layers)
+
+
+def launches_per_generation(n_layers: int, new_tokens: int, prefill_tokens: int) -> int:
+    """minitp_b200 kernel launches of one fixed-length generation."""
+    prefill = 1 + n_layers * 5 + (2 * n_layers + 1 if prefill_tokens > 1 else 0) + 1
+    select = 2  # argmax rows + finish
+    seed = 1  # decode position store
+    step = 1 + 5 * n_layers + 1 + 1
+    return prefill + select + seed + (new_tokens - 1) * step
+
+
+# ---------------------------------------------------------------------- #
+# CPU baseline (oracle port of the reference)
+# ---------------------------------------------------------------------- #
+def cpu_oracle_decode(cfg, batch, prompt_len, sample_tokens, dtype, tp, threads):
+    from oracle.model import OracleConfig, OracleModel, checkpoint_tensors, prompt
+
+    torch.set_num_threads(threads)
+    model = OracleModel(OracleConfig.of(cfg), checkpoint_tensors(cfg), tp=tp, dtype=dtype)
+    ids = prompt(cfg.vocab_size, batch, prompt_len)
+    model.reset(batch, prompt_len + sample_tokens + 1)
+    logits = model.forward(ids, torch.arange(prompt_len))
+    tok = model.select(logits[:, -1])
+    t0 = time.perf_counter()
+    for i in range(sample_tokens):
+        logits = model.forward(tok[:, None], torch.tensor([prompt_len + i]))
+        tok = model.select(logits[:, -1])
+    dt = time.perf_counter() - t0
+    return batch * sample_tokens / dt, dt
+
+
+def run_reference(args, cfg, prompt_len, new_tokens):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    sample = 8
+    vals = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_oracle_decode(cfg, args.batch, prompt_len, 2, dtype, args.gpus, threads)
+    for _ in range(args.steps):
+        v, _ = cpu_oracle_decode(cfg, args.batch, prompt_len, sample, dtype, args.gpus, threads)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": "decode tok/s", "value": round(value, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * args.batch / value, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded random weights and prompts)",
+        "config": {"workload": f"{args.model} B={args.batch} P={prompt_len} new={new_tokens} tp={args.gpus}",
+                   "model": args.model, "global_batch": args.batch, "seq_len": prompt_len + new_tokens,
+                   "parallelism": f"tp{args.gpus} (emulated in one process)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"prefill {prompt_len} + {sample} decode tokens per step, oracle port of "
+                                   f"the reference CPU path, tp={args.gpus} emulated"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- #
+# B200 arm
+# ---------------------------------------------------------------------- #
+def run_b200(args, cfg, prompt_len, new_tokens):
+    import torch.distributed as dist
+
+    from minitp_b200 import _lib, ops
+    from minitp_b200.build import build
+    from minitp_b200.distributed.context import init_context
+    from minitp_b200.generation import GenerationState, generate_greedy
+    from minitp_b200.synthetic import make_prompt
+    from minitp_b200.weight_loader import load_synthetic_tp
+
+    if int(os.environ.get("RANK", "0")) == 0:
+        build()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        # rank 0 built the library; the others wait for it through the store
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    ctx = init_context(timeout_s=120.0)
+    if world > 1:
+        dist.barrier()
+    lib = _lib.load()
+    if args.no_pdl:
+        lib.mtpb_set_pdl(0)
+    dev = ctx.device
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    gen_dev = args.gen_device or ("cuda" if args.model == "qwen2.5-7b" else "cpu")
+    model = load_synthetic_tp(cfg, ctx, dtype=dtype, device=dev, seed=0, gen_device=gen_dev)
+    ids_host = make_prompt(cfg.vocab_size, args.batch, prompt_len).pin_memory()
+    ids = ids_host.to(dev)
+    comm = ctx.comm()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def one_step(timed: bool):
+        st = GenerationState(model, ids, new_tokens)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        logits = st.prefill(last_only=True)
+        tok = st.select_next(logits)
+        st.append(tok)
+        st.start_device_decode(tok)
+        st.device_step()
+        st.capture()
+        ev[1].record()
+        for _ in range(new_tokens - 2):
+            st.graph_step()
+        ev[2].record()
+        return st, ev
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        one_step(False)
+        flush.zero_()
+    barrier()
+    comm.raise_on_error()
+
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
+    decode_ms, step_ms = [], []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()  # L2 flush between timed steps (256 MiB > 126 MB L2)
+        st, ev = one_step(True)
+        torch.cuda.synchronize()
+        decode_ms.append(ev[1].elapsed_time(ev[2]) / max(1, new_tokens - 2))
+        step_ms.append(ev[0].elapsed_time(ev[2]))
+        st.release()
+    barrier()
+    clocks = sampler.stop()
+    comm.raise_on_error()
+
+    # max over ranks
+    t = torch.tensor([statistics.mean(decode_ms), statistics.mean(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_token, ms_per_step = t.tolist()
+    value = args.batch / (ms_per_token / 1e3)
+
+    # e2e through the public API: pinned host ids in, host ids out
+    e2e_ms = []
+    for _ in range(max(2, min(args.steps, 5))):
+        flush.zero_()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = generate_greedy(model, ids_host.to(dev, non_blocking=True), new_tokens, early_stop=False)
+        host = out.to("cpu", non_blocking=False)
+        e.record()
+        torch.cuda.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    te = torch.tensor([statistics.mean(e2e_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = args.batch * new_tokens / (te.item() / 1e3)
+
+    # dominant kernel, timed live: the LM-head GEMV over this rank's vocab shard
+    x = torch.randn(args.batch, cfg.hidden_size, device=dev).to(dtype)
+    w = model.lm_head.weight
+    for _ in range(3):
+        ops.linear(x, w)
+    reps = 50
+    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush.zero_()
+    torch.cuda.synchronize()
+    ks.record()
+    for _ in range(reps):
+        ops.linear(x, w)
+    ke.record()
+    torch.cuda.synchronize()
+    k_ms = ks.elapsed_time(ke) / reps
+    peak, peak_kind = peaks()
+    k_bytes = w.numel() * w.element_size() + x.numel() * x.element_size() + args.batch * w.shape[0] * w.element_size()
+    k_gbs = k_bytes / (k_ms / 1e3) / 1e9
+
+    wb = weight_bytes_per_token(model)
+    kvb = kv_bytes_per_token(model, args.batch, prompt_len + new_tokens / 2)
+    tok_gbs = (wb + kvb) / (ms_per_token / 1e3) / 1e9
+
+    line = None
+    if ctx.is_rank_zero:
+        line = {
+            "metric": "decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "us_per_token": round(ms_per_token * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.dtype,
+            "data": "synthetic (seeded random weights N(0,0.02) and uniform prompt ids)",
+            "config": {
+                "workload": f"{args.model} decode, B={args.batch}, prompt {prompt_len}, {new_tokens} new tokens, "
+                            f"TP={world}",
+                "model": args.model, "global_batch": args.batch, "seq_len": prompt_len + new_tokens,
+                "parallelism": f"tp{world}", "heads_padded": bool(model.cfg.is_padded),
+                "l2": "flushed between timed steps (256 MiB write)",
+                "decode": "CUDA graph replay of the device-resident decode step, PDL chained kernels",
+            },
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
+                    "d2h_bytes_per_step": args.batch * (prompt_len + new_tokens) * 8,
+                    "definition": "generate_greedy from pinned host ids to host output ids, incl. prefill"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel (LM head, vocab shard)",
+                         "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(k_gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_launch": k_bytes, "us_per_launch": round(k_ms * 1e3, 3)},
+            "roofline_token": {"bound": "hbm", "achieved": round(tok_gbs, 1), "peak": peak, "unit": "GB/s",
+                               "frac": round(tok_gbs / peak, 4), "weight_bytes": wb, "kv_bytes": round(kvb),
+                               "peak_kind": peak_kind},
+            "gpu_launches": launches_per_generation(cfg.num_hidden_layers, new_tokens, prompt_len) * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            v, dt = cpu_oracle_decode(cfg, args.batch, prompt_len, 8, dtype, 1, threads)
+            line["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                                    "sample": f"prefill {prompt_len} + 8 decode tokens ({dt:.1f} s), "
+                                              "oracle port of the reference CPU path"}
+    if world > 1:
+        dist.barrier()
+    model.release_native()
+    if line is not None:
+        s = json.dumps(line)
+        print(s, flush=True)
+        if args.out:
+            with open(args.out, "w") as f:
+                f.write(s + "\n")
+    ctx.destroy()
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    cfg, prompt_len, new_tokens = workload(args)
+    if args.impl == "reference":
+        run_reference(args, cfg, prompt_len, new_tokens)
+    else:
+        run_b200(args, cfg, prompt_len, new_tokens)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+// Split-KV grouped-query attention over the rank's local heads.
+//
+// Row m of q is token t = m % tpr of batch row b = m / tpr at absolute
+// position pos = pos0 + t (pos0 from device memory in the captured decode
+// step). It attends to cache positions [0, pos] of its KV head: the causal
+// rule of the reference for decode (no mask), prefill (is_causal) and chunked
+// prefill (tril(diagonal=cache_len)). The `G = hq / hkv` query heads sharing
+// one KV head are processed by the same CTA, so K/V bytes are read once per
+// group (no expand / repeat_interleave copies).
+//
+// grid = (nsplit, hkv, M); each CTA covers one contiguous slice of the
+// positions. With nsplit > 1 the partial softmax states (max, sum, o) go to
+// scratch and the last CTA of each (row, kv head) merges them.
+#pragma once
+
+#include "comm.cuh"
+
+namespace mtpb {
+
+struct AttnParams {
+  const void* q;  // [M][hq*hd]
+  const void* k_cache;
+  const void* v_cache;  // [B][hkv][cap][hd]
+  void* out;            // [M][hq*hd]
+  int M, tpr, hq, hkv, cap;
+  const int* pos_ptr;
+  int pos_base;
+  float scale;
+  int nsplit;
+  int chunk_cap;  // max positions per split (sizes the score buffer)
+  float* part_o;  // [M][hq][nsplit][hd]
+  float* part_ml;  // [M][hq][nsplit][2]
+  uint32_t* counters;  // [M][hkv], zero between launches
+  uint32_t* status;
+};
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnGB = 4;  // heads per PV pass
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) {
+  constexpr int VE = VecTraits<T>::kElems;
+  constexpr int LPP = HD / VE;  // lanes per key row
+  static_assert(LPP >= 1 && LPP <= 32 && (32 % LPP) == 0, "unsupported head_dim");
+  constexpr int PPW = 32 / LPP;  // key rows per warp pass
+  constexpr int DCH = HD / VE;   // 16-byte chunks per row
+  constexpr int NW = kAttnThreads / 32;
+  constexpr int NPL = kAttnThreads / DCH;  // position lanes in the PV pass
+
+  extern __shared__ __align__(16) float sm[];
+  const int G = p.hq / p.hkv;
+  float* qf = sm;                       // [G][HD]
+  float* sc = qf + G * HD;              // [G][chunk_cap]
+  float* ml = sc + G * p.chunk_cap;     // [G][2]
+  float* ro = ml + 2 * G;               // [NPL][kAttnGB][HD]
+  __shared__ int s_last;
+
+  pdl_launch();
+  pdl_wait();
+
+  const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+  const int b = m / p.tpr, t = m - b * p.tpr;
+  const int pos = (p.pos_ptr ? *p.pos_ptr : p.pos_base) + t;
+  if (pos < 0 || pos >= p.cap) {
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusBadPosition);
+    return;
+  }
+  const int L = pos + 1;
+  const int chunk = (L + p.nsplit - 1) / p.nsplit;
+  const int s0 = min(L, split * chunk), s1 = min(L, s0 + chunk);
+  const int n = s1 - s0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const T* kbase = static_cast<const T*>(p.k_cache) + (size_t(b) * p.hkv + kvh) * p.cap * HD;
+  const T* vbase = static_cast<const T*>(p.v_cache) + (size_t(b) * p.hkv + kvh) * p.cap * HD;
+  const T* qrow = static_cast<const T*>(p.q) + size_t(m) * p.hq * HD + size_t(kvh) * G * HD;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qf[i] = to_f(qrow[i]);
+  __syncthreads();
+
+  // scores: LPP lanes per key row, PPW rows per warp pass
+  {
+    const int pg = lane / LPP, li = lane - pg * LPP;
+    for (int r0 = s0 + warp * PPW; r0 < s1; r0 += NW * PPW) {
+      const int r = r0 + pg;
+      const bool ok = r < s1;
+      float kf[VE];
+      unpack(ok ? ld_vec(kbase + size_t(r) * HD + li * VE) : make_uint4(0, 0, 0, 0), kf);
+      for (int g = 0; g < G; ++g) {
+        const float* qg = qf + g * HD + li * VE;
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) d = fmaf(kf[e], qg[e], d);
+#pragma unroll
+        for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (ok && li == 0) sc[g * p.chunk_cap + (r - s0)] = d * p.scale;
+      }
+    }
+  }
+  __syncthreads();
+
+  // softmax statistics per head (one warp per head)
+  for (int g = warp; g < G; g += NW) {
+    float* s = sc + g * p.chunk_cap;
+    float mx = -INFINITY;
+    for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float e = expf(s[i] - mx);
+      s[i] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      ml[2 * g] = mx;
+      ml[2 * g + 1] = sum;
+    }
+  }
+  __syncthreads();
+
+  // o[g][:] = sum_r p[g][r] * v[r][:], kAttnGB heads per pass
+  const int dc = threadIdx.x % DCH, pl = threadIdx.x / DCH;
+  const bool single = p.nsplit == 1;
+  for (int g0 = 0; g0 < G; g0 += kAttnGB) {
+    float acc[kAttnGB][VE];
+#pragma unroll
+    for (int gg = 0; gg < kAttnGB; ++gg)
+#pragma unroll
+      for (int e = 0; e < VE; ++e) acc[gg][e] = 0.f;
+    for (int r = pl; r < n; r += NPL) {
+      float vf[VE];
+      unpack(ld_vec(vbase + size_t(s0 + r) * HD + dc * VE), vf);
+#pragma unroll
+      for (int gg = 0; gg < kAttnGB; ++gg) {
+        if (g0 + gg < G) {
+          const float pr = sc[(g0 + gg) * p.chunk_cap + r];
+#pragma unroll
+          for (int e = 0; e < VE; ++e) acc[gg][e] = fmaf(pr, vf[e], acc[gg][e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int gg = 0; gg < kAttnGB; ++gg)
+#pragma unroll
+      for (int e = 0; e < VE; ++e) ro[(pl * kAttnGB + gg) * HD + dc * VE + e] = acc[gg][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < kAttnGB * HD; i += blockDim.x) {
+      const int gg = i / HD, d = i - gg * HD;
+      const int g = g0 + gg;
+      if (g < G) {
+        float o = 0.f;
+        for (int q = 0; q < NPL; ++q) o += ro[(q * kAttnGB + gg) * HD + d];
+        const int head = kvh * G + g;
+        if (single) {
+          static_cast<T*>(p.out)[size_t(m) * p.hq * HD + size_t(head) * HD + d] =
+              from_f<T>(o / ml[2 * g + 1]);
+        } else {
+          p.part_o[((size_t(m) * p.hq + head) * p.nsplit + split) * HD + d] = o;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (single) return;
+
+  // publish (max, sum) and merge in the last CTA of this (row, kv head)
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    const int head = kvh * G + g;
+    float* d = p.part_ml + ((size_t(m) * p.hq + head) * p.nsplit + split) * 2;
+    d[0] = n > 0 ? ml[2 * g] : -INFINITY;
+    d[1] = n > 0 ? ml[2 * g + 1] : 0.f;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* ctr = p.counters + size_t(m) * p.hkv + kvh;
+    const uint32_t old = atomicAdd(ctr, 1u);
+    s_last = old == uint32_t(p.nsplit - 1);
+    if (s_last) *ctr = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i - g * HD;
+    const int head = kvh * G + g;
+    const float* mlh = p.part_ml + (size_t(m) * p.hq + head) * p.nsplit * 2;
+    const float* oh = p.part_o + (size_t(m) * p.hq + head) * p.nsplit * HD;
+    float mx = -INFINITY;
+    for (int s = 0; s < p.nsplit; ++s) mx = fmaxf(mx, __ldcg(mlh + 2 * s));
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float ms = __ldcg(mlh + 2 * s);
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - mx);
+      num = fmaf(w, __ldcg(oh + size_t(s) * HD + d), num);
+      den = fmaf(w, __ldcg(mlh + 2 * s + 1), den);
+    }
+    static_cast<T*>(p.out)[size_t(m) * p.hq * HD + size_t(head) * HD + d] = from_f<T>(num / den);
+  }
+}
+
+}  // namespace mtpb

@@ -1,0 +1,1040 @@
+// C ABI of libminitp_b200.so (declared in include/minitp_b200.h): launch
+// configuration, the NVLink communicator, standalone operators and the model
+// sequencer that chains the kernels of one forward / one decode step.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "minitp_b200.h"
+#include "misc.cuh"
+
+using namespace mtpb;
+
+namespace {
+
+thread_local std::string g_err;
+bool g_pdl = true;
+uint32_t g_prefetch_cap = 4u << 20;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(MTPB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define MTPB_CUDA(call)                                 \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return fail_cuda(e_, #call); \
+  } while (0)
+#define MTPB_TRY(call)         \
+  do {                         \
+    int r_ = (call);           \
+    if (r_ != MTPB_OK) return r_; \
+  } while (0)
+
+size_t dsize(int dtype) { return dtype == MTPB_BF16 ? 2 : 4; }
+int vec_elems(int dtype) { return dtype == MTPB_BF16 ? 8 : 4; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <typename Kern, typename Param>
+int launch(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, const Param& prm) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  if (smem > 48 * 1024) {
+    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  }
+  MTPB_CUDA(cudaLaunchKernelEx(&cfg, kern, prm));
+  return MTPB_OK;
+}
+
+// ------------------------------------------------------------------ comm
+struct CommHost {
+  Comm dev;
+  void* local = nullptr;
+  void* mapped[kMaxRanks] = {};
+  int device = 0;
+  bool open = false;
+};
+
+// A communicator-less call still needs control words and a local slot: a
+// lazily created world-1 communicator per device serves those.
+CommHost* default_comm() {
+  static std::mutex mu;
+  static CommHost* per_dev[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!per_dev[dev]) {
+    void* c = nullptr;
+    if (mtpb_comm_create(0, 1, 1u << 20, &c) != MTPB_OK) return nullptr;
+    per_dev[dev] = static_cast<CommHost*>(c);
+  }
+  return per_dev[dev];
+}
+
+CommHost* as_comm(void* c) { return c ? static_cast<CommHost*>(c) : default_comm(); }
+
+// ------------------------------------------------------------------ GEMV launch
+constexpr size_t kXsStageMax = 64 * 1024;  // x staged in smem up to this size
+
+template <typename T, int EPI>
+int gemv_launch(GemvParams p, cudaStream_t st) {
+  constexpr int UR = EpiTraits<EPI>::kUR;
+  constexpr int RPW = kRowsPerWarp / UR;
+  constexpr int VE = VecTraits<T>::kElems;
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return fail(MTPB_ERR_INVALID, "gemv: empty shape");
+  if (p.K % VE != 0 || !aligned16(p.w)) {
+    return fail(MTPB_ERR_INVALID, "gemv: K * sizeof(dtype) must be a multiple of 16 bytes and w 16-byte aligned");
+  }
+  if (p.x_mode == 0 && (!aligned16(p.x) || (size_t(p.ldx) * sizeof(T)) % 16 != 0)) {
+    return fail(MTPB_ERR_INVALID, "gemv: x must be 16-byte aligned with a 16-byte row stride");
+  }
+  if (EPI == kEpiArgmax && p.M > 64) return fail(MTPB_ERR_INVALID, "gemv argmax: M > 64");
+  const int sms = sm_count();
+  const int G = std::max(1, std::min(p.units, std::min(sms, kMaxCtas)));
+  const int per = (p.units + G - 1) / G;
+  const int groups = (per + RPW - 1) / RPW;
+  const int CPR = p.K / VE;
+  int ks = 1;
+  while (ks < kGemvWarps && groups * ks * 2 <= kGemvWarps && CPR / (ks * 2) >= 16) ks *= 2;
+  p.ks = ks;
+  const size_t xbytes = size_t(p.M) * p.K * sizeof(T);
+  if (p.x_mode == 1) {
+    if (xbytes > 200 * 1024) return fail(MTPB_ERR_INVALID, "gemv consume: x does not fit in shared memory");
+    p.x_smem = 1;
+  } else {
+    p.x_smem = xbytes <= kXsStageMax ? 1 : 0;
+  }
+  p.prefetch_cap = g_prefetch_cap;
+  const size_t smem = (p.x_smem ? xbytes : 0) + size_t(kGemvWarps) * 32 * 2 * sizeof(float);
+  const int MT = p.M >= 8 ? 8 : p.M >= 4 ? 4 : p.M >= 2 ? 2 : 1;
+  switch (MT) {
+    case 1: return launch(gemv_kernel<T, EPI, 1>, dim3(G), dim3(kGemvThreads), smem, st, p);
+    case 2: return launch(gemv_kernel<T, EPI, 2>, dim3(G), dim3(kGemvThreads), smem, st, p);
+    case 4: return launch(gemv_kernel<T, EPI, 4>, dim3(G), dim3(kGemvThreads), smem, st, p);
+    default: return launch(gemv_kernel<T, EPI, 8>, dim3(G), dim3(kGemvThreads), smem, st, p);
+  }
+}
+
+template <int EPI>
+int gemv_dispatch(int dtype, const GemvParams& p, cudaStream_t st) {
+  if (dtype == MTPB_BF16) return gemv_launch<bf16, EPI>(p, st);
+  if (dtype == MTPB_F32) return gemv_launch<float, EPI>(p, st);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+// grid size a GEMV launch will use (producer CTA count of a push site)
+int gemv_grid(int units) { return std::max(1, std::min(units, std::min(sm_count(), kMaxCtas))); }
+
+GemvParams gemv_base(const void* w, const void* bias, int M, int N, int K, int units) {
+  GemvParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.w = w;
+  p.bias = bias;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.units = units;
+  p.tpr = 1;
+  return p;
+}
+
+// ------------------------------------------------------------------ attention launch
+constexpr size_t kAttnSmemMax = 160 * 1024;
+
+struct AttnScratch {
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  uint32_t* counters = nullptr;
+  size_t o_elems = 0, ml_elems = 0, ctr_elems = 0;
+};
+
+int attn_choose_splits(int M, int hkv, int G, int cap, int hd, int* chunk_cap) {
+  const int sms = sm_count();
+  int ns = 1;
+  // fill the GPU: (rows x kv heads x splits) >= SMs, but keep >= 64 keys per split
+  while (M * hkv * ns < sms && (cap + ns * 2 - 1) / (ns * 2) >= 64) ns *= 2;
+  // bound the score buffer in shared memory
+  auto smem_of = [&](int s) {
+    const int cc = (cap + s - 1) / s;
+    return size_t(G) * hd * 4 + size_t(G) * cc * 4 + size_t(G) * 8 + 16 * 1024 + 64;
+  };
+  while (smem_of(ns) > kAttnSmemMax) ns *= 2;
+  *chunk_cap = (cap + ns - 1) / ns;
+  return ns;
+}
+
+template <typename T>
+int attn_launch_t(AttnParams p, int hd, cudaStream_t st) {
+  const int G = p.hq / p.hkv;
+  const size_t smem = size_t(G) * hd * 4 + size_t(G) * p.chunk_cap * 4 + size_t(G) * 8 + 16 * 1024 + 64;
+  dim3 grid(p.nsplit, p.hkv, p.M);
+  switch (hd) {
+    case 16: return launch(attn_kernel<T, 16>, grid, dim3(kAttnThreads), smem, st, p);
+    case 32: return launch(attn_kernel<T, 32>, grid, dim3(kAttnThreads), smem, st, p);
+    case 64: return launch(attn_kernel<T, 64>, grid, dim3(kAttnThreads), smem, st, p);
+    case 128: return launch(attn_kernel<T, 128>, grid, dim3(kAttnThreads), smem, st, p);
+    default: return fail(MTPB_ERR_INVALID, "attention: head_dim must be 16, 32, 64 or 128");
+  }
+}
+
+int attn_run(int dtype, const void* q, const void* kc, const void* vc, void* out, int B, int T, int hq,
+             int hkv, int hd, int cap, const int* pos_ptr, int pos_base, AttnScratch& scr,
+             uint32_t* status, cudaStream_t st) {
+  if (hq % hkv != 0) return fail(MTPB_ERR_INVALID, "attention: hq must be a multiple of hkv");
+  const int G = hq / hkv;
+  if (G > 64) return fail(MTPB_ERR_INVALID, "attention: more than 64 query heads per KV head");
+  if (B * T > 65535 || hkv > 65535) return fail(MTPB_ERR_INVALID, "attention: more than 65535 rows per launch");
+  if (dtype == MTPB_F32 && hd < 16) return fail(MTPB_ERR_INVALID, "attention: head_dim too small");
+  const int M = B * T;
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.k_cache = kc;
+  p.v_cache = vc;
+  p.out = out;
+  p.M = M;
+  p.tpr = T;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.cap = cap;
+  p.pos_ptr = pos_ptr;
+  p.pos_base = pos_base;
+  p.scale = 1.0f / std::sqrt(float(hd));
+  p.nsplit = attn_choose_splits(M, hkv, G, cap, hd, &p.chunk_cap);
+  p.status = status;
+  if (p.nsplit > 1) {
+    const size_t need_o = size_t(M) * hq * p.nsplit * hd, need_ml = size_t(M) * hq * p.nsplit * 2,
+                 need_c = size_t(M) * hkv;
+    if (need_o > scr.o_elems || need_ml > scr.ml_elems || need_c > scr.ctr_elems) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs != cudaStreamCaptureStatusNone)
+        return fail(MTPB_ERR_INVALID, "attention scratch must be reserved before graph capture");
+      cudaFree(scr.part_o);
+      cudaFree(scr.part_ml);
+      cudaFree(scr.counters);
+      MTPB_CUDA(cudaMalloc(&scr.part_o, need_o * 4));
+      MTPB_CUDA(cudaMalloc(&scr.part_ml, need_ml * 4));
+      MTPB_CUDA(cudaMalloc(&scr.counters, need_c * 4));
+      MTPB_CUDA(cudaMemsetAsync(scr.counters, 0, need_c * 4, st));
+      scr.o_elems = need_o;
+      scr.ml_elems = need_ml;
+      scr.ctr_elems = need_c;
+    }
+    p.part_o = scr.part_o;
+    p.part_ml = scr.part_ml;
+    p.counters = scr.counters;
+  }
+  if (dtype == MTPB_BF16) return attn_launch_t<bf16>(p, hd, st);
+  if (dtype == MTPB_F32) return attn_launch_t<float>(p, hd, st);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+AttnScratch& standalone_attn_scratch() {
+  static AttnScratch s[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return s[dev];
+}
+
+// ------------------------------------------------------------------ small launches
+template <typename T>
+int embed_launch(const EmbedParams& p, int grid, cudaStream_t st) {
+  return launch(embed_kernel<T>, dim3(grid), dim3(128), 0, st, p);
+}
+int embed_run(int dtype, const EmbedParams& p, int grid, cudaStream_t st) {
+  if (dtype == MTPB_BF16) return embed_launch<bf16>(p, grid, st);
+  if (dtype == MTPB_F32) return embed_launch<float>(p, grid, st);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+int ar_norm_run(int dtype, ArNormParams p, cudaStream_t st) {
+  if (size_t(p.rows) * p.H * dsize(dtype) > p.comm.slot_bytes && p.comm.world > 1)
+    return fail(MTPB_ERR_INVALID, "allreduce: message larger than the communicator slot");
+  // rows per CTA: spread rows over the SMs, at most kMaxCtas CTAs
+  const int sms = sm_count();
+  int ctas = std::min(p.rows, std::min(sms * 2, kMaxCtas));
+  ctas = std::max(ctas, 1);
+  p.rpc = (p.rows + ctas - 1) / ctas;
+  ctas = (p.rows + p.rpc - 1) / p.rpc;
+  if (dtype == MTPB_BF16) return launch(ar_norm_kernel<bf16>, dim3(ctas), dim3(256), 0, st, p);
+  if (dtype == MTPB_F32) return launch(ar_norm_kernel<float>, dim3(ctas), dim3(256), 0, st, p);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+int argmax_splits(int V) { return std::max(1, std::min(64, (V + 4095) / 4096)); }
+
+int argmax_rows_run(int dtype, const ArgmaxRowsParams& p, cudaStream_t st) {
+  dim3 grid(argmax_splits(p.V), p.M);
+  if (dtype == MTPB_BF16) return launch(argmax_rows_kernel<bf16>, grid, dim3(256), 0, st, p);
+  if (dtype == MTPB_F32) return launch(argmax_rows_kernel<float>, grid, dim3(256), 0, st, p);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+// a consumer-only pass for the model channel when x does not fit in shared
+// memory: it reduces a collective site into res_out and the normalised xn.
+struct ConsumeRowsParams {
+  GemvParams g;  // x_mode-1 fields (comm, seq, res_in, res_out, gain, eps, M, K = H)
+  void* xn;      // [M][H]
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) consume_rows_kernel(const ConsumeRowsParams cp) {
+  __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
+  const GemvParams& p = cp.g;
+  const Comm& c = p.comm;
+  const uint32_t seq = resolve_seq(c, p.in_seq);
+  if (!wait_peers(c, p.in_chan, seq, p.in_nprod)) return;
+  const int par = seq & 1;
+  const int H = p.K;
+  const T* gain = static_cast<const T*>(p.gain);
+  T* xn = static_cast<T*>(cp.xn);
+  for (int m = blockIdx.x; m < p.M; m += gridDim.x) {
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+      const size_t off = size_t(m) * H + j;
+      float s = 0.f;
+      for (int r = 0; r < c.world; ++r) s += to_f(__ldcg(reinterpret_cast<const T*>(c.data(c.rank, p.in_chan, par, r)) + off));
+      float o = round_t<T>(s);
+      if (p.ar_bias) o = round_t<T>(o + to_f(static_cast<const T*>(p.ar_bias)[j]));
+      float x = o;
+      if (p.has_res) x = round_t<T>(to_f(static_cast<const T*>(p.res_in)[off]) + o);
+      static_cast<T*>(p.res_out)[off] = from_f<T>(x);
+      ss += x * x;
+    }
+    const float tot = block_sum(ss, red);
+    const float rinv = rsqrtf(tot / float(H) + p.eps);
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+      const size_t off = size_t(m) * H + j;
+      const float x = to_f(static_cast<const T*>(p.res_out)[off]);
+      xn[off] = from_f<T>(__fmul_rn(__fmul_rn(x, rinv), to_f(gain[j])));
+    }
+    __syncthreads();
+  }
+}
+
+int consume_rows_run(int dtype, const ConsumeRowsParams& cp, cudaStream_t st) {
+  const int grid = std::max(1, std::min(cp.g.M, sm_count() * 2));
+  if (dtype == MTPB_BF16) return launch(consume_rows_kernel<bf16>, dim3(grid), dim3(256), 0, st, cp);
+  if (dtype == MTPB_F32) return launch(consume_rows_kernel<float>, dim3(grid), dim3(256), 0, st, cp);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+// ------------------------------------------------------------------ model
+struct ModelHost {
+  mtpb_model_desc d;
+  std::vector<mtpb_layer_desc> layers;
+  CommHost* comm = nullptr;
+  int reserved_rows = 0;
+  char* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  void* q = nullptr;
+  void* attn = nullptr;
+  void* act = nullptr;
+  void* res[2] = {nullptr, nullptr};
+  void* xn = nullptr;
+  void* logits = nullptr;  // [64][V_local] scratch for decode steps without a logits output
+  long long* best = nullptr;
+  AttnScratch ascr;
+};
+
+bool capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  return cs != cudaStreamCaptureStatusNone;
+}
+
+int model_reserve(ModelHost& mh, int rows, cudaStream_t st) {
+  if (rows <= mh.reserved_rows) return MTPB_OK;
+  if (capturing(st)) return fail(MTPB_ERR_INVALID, "model scratch must be reserved before graph capture");
+  const mtpb_model_desc& d = mh.d;
+  const size_t es = dsize(d.dtype);
+  const size_t qb = size_t(rows) * d.hq_local * d.head_dim * es;
+  const size_t ab = size_t(rows) * d.inter_local * es;
+  const size_t hb = size_t(rows) * d.hidden * es;
+  const size_t lb = size_t(64) * size_t(d.vocab_end - d.vocab_start) * es;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t total = up(qb) * 2 + up(ab) + up(hb) * 3 + up(lb) + 64 * 8;
+  cudaFree(mh.scratch);
+  mh.scratch = nullptr;
+  MTPB_CUDA(cudaMalloc(&mh.scratch, total));
+  char* p = mh.scratch;
+  mh.q = p; p += up(qb);
+  mh.attn = p; p += up(qb);
+  mh.act = p; p += up(ab);
+  mh.res[0] = p; p += up(hb);
+  mh.res[1] = p; p += up(hb);
+  mh.xn = p; p += up(hb);
+  mh.logits = p; p += up(lb);
+  mh.best = reinterpret_cast<long long*>(p);
+  std::vector<long long> init(64, kArgmaxEmpty);
+  MTPB_CUDA(cudaMemcpy(mh.best, init.data(), 64 * 8, cudaMemcpyHostToDevice));
+  mh.scratch_bytes = total;
+  mh.reserved_rows = rows;
+  return MTPB_OK;
+}
+
+struct FwdArgs {
+  const long long* ids;  // embedding input [M]
+  int B, T;
+  const long long* rope_pos;
+  int cache_len;        // slot of token 0 (when pos_ptr is null)
+  int* pos_ptr;         // device slot of token 0 (decode step)
+  void* const* kc;
+  void* const* vc;
+  int cap;
+  void* logits;
+  int last_only;
+  bool decode;          // distributed argmax + token write + position advance
+  long long* tok_out;
+  long long* out_ids;
+  int ld_out;
+};
+
+// One forward over tokens [t0, t0 + tc) of every batch row (a chunk of the
+// caller's T tokens). Every collective payload is B * tc * H elements, which
+// the caller sized to fit one communicator slot.
+template <typename T>
+int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chunk, cudaStream_t st) {
+  const mtpb_model_desc& d = mh.d;
+  const Comm& comm = mh.comm->dev;
+  const int L = d.n_layers, H = d.hidden, hd = d.head_dim;
+  const int hq = d.hq_local, hkv = d.hkv_local;
+  const int M = a.B * tc;
+  const int qrows = (hq + 2 * hkv) * hd;
+  const int vloc = int(d.vocab_end - d.vocab_start);
+  const uint32_t nsite = uint32_t(2 * L + 2);
+  const bool chunked = tc != a.T;
+  const bool fused_x = size_t(M) * H * sizeof(T) <= kXsStageMax && tc == 1;
+  const int chan = 0;
+  const int pos_base = a.cache_len + t0;
+  const long long* rope_pos = a.rope_pos ? a.rope_pos + t0 : nullptr;
+
+  // embedding -> site 0 (opens a new step of channel 0)
+  const int egrid = std::max(1, std::min(M, 64));
+  {
+    EmbedParams e;
+    std::memset(&e, 0, sizeof(e));
+    e.ids = a.ids;
+    if (chunked) {
+      e.ids_tpr = tc;
+      e.ids_T = a.T;
+      e.ids_t0 = t0;
+    }
+    e.table = d.embed;
+    e.M = M;
+    e.H = H;
+    e.vstart = d.vocab_start;
+    e.vend = d.vocab_end;
+    e.vtotal = d.vocab_size;
+    e.comm = comm;
+    e.chan = chan;
+    e.seq = SeqRef{0u, nsite, 0u};
+    e.advance_step = 1;
+    MTPB_TRY(embed_run(d.dtype, e, egrid, st));
+  }
+  int nprod = egrid;
+  int cur = 0;  // residual ping-pong index holding the current residual
+  bool has_res = false;
+  const int grid_o = gemv_grid(H), grid_down = gemv_grid(H);
+
+  auto consume_into = [&](GemvParams& g, uint32_t site, const void* gain) {
+    g.comm = comm;
+    g.in_seq = SeqRef{site, nsite, 0u};
+    g.in_chan = chan;
+    g.in_nprod = nprod;
+    g.res_in = has_res ? mh.res[cur] : nullptr;
+    g.res_out = mh.res[has_res ? 1 - cur : cur];
+    g.gain = gain;
+    g.eps = d.eps;
+    g.has_res = has_res ? 1 : 0;
+  };
+  auto after_consume = [&]() {
+    if (has_res) cur = 1 - cur;
+    has_res = true;
+  };
+  // consume site `site` + RMSNorm, either fused into the GEMV `g` (x in
+  // shared memory) or as a separate pass that writes mh.xn
+  auto prepare_input = [&](GemvParams& g, uint32_t site, const void* gain, bool allow_fused) -> int {
+    consume_into(g, site, gain);
+    if (fused_x && allow_fused) {
+      g.x_mode = 1;
+    } else {
+      ConsumeRowsParams cp;
+      cp.g = g;
+      cp.g.M = M;
+      cp.g.K = H;
+      cp.xn = mh.xn;
+      MTPB_TRY(consume_rows_run(d.dtype, cp, st));
+      g.x_mode = 0;
+      g.x = mh.xn;
+      g.ldx = H;
+    }
+    after_consume();
+    return MTPB_OK;
+  };
+
+  for (int l = 0; l < L; ++l) {
+    const mtpb_layer_desc& ly = mh.layers[l];
+    // fused QKV + RoPE + KV append, consuming site 2l (embedding or previous down)
+    {
+      GemvParams g = gemv_base(ly.qkv_w, ly.qkv_b, M, qrows, H, qrows / 2);
+      MTPB_TRY(prepare_input(g, uint32_t(2 * l), ly.ln1, true));
+      g.y = mh.q;
+      g.ldy = hq * hd;
+      g.cos_tab = d.cos_tab;
+      g.sin_tab = d.sin_tab;
+      g.rope_len = d.rope_len;
+      g.hd = hd;
+      g.hq = hq;
+      g.hkv = hkv;
+      g.k_cache = a.kc[l];
+      g.v_cache = a.vc[l];
+      g.kv_cap = a.cap;
+      g.tpr = tc;
+      g.pos_ptr = a.pos_ptr;
+      g.pos_base = pos_base;
+      g.rope_pos = rope_pos;
+      MTPB_TRY(gemv_dispatch<kEpiRope>(d.dtype, g, st));
+    }
+    // attention over the cache
+    MTPB_TRY(attn_run(d.dtype, mh.q, a.kc[l], a.vc[l], mh.attn, a.B, tc, hq, hkv, hd, a.cap, a.pos_ptr,
+                      pos_base, mh.ascr, comm.status(), st));
+    // o_proj partial -> push site 2l+1
+    {
+      GemvParams g = gemv_base(ly.o_w, nullptr, M, H, hq * hd, H);
+      g.x = mh.attn;
+      g.ldx = hq * hd;
+      g.comm = comm;
+      g.out_seq = SeqRef{uint32_t(2 * l + 1), nsite, 0u};
+      g.out_chan = chan;
+      MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
+      nprod = grid_o;
+    }
+    // gate/up + SwiGLU, consuming site 2l+1
+    {
+      GemvParams g = gemv_base(ly.gu_w, nullptr, M, 2 * d.inter_local, H, d.inter_local);
+      MTPB_TRY(prepare_input(g, uint32_t(2 * l + 1), ly.ln2, true));
+      g.y = mh.act;
+      g.ldy = d.inter_local;
+      MTPB_TRY(gemv_dispatch<kEpiSwiglu>(d.dtype, g, st));
+    }
+    // down partial -> push site 2l+2
+    {
+      GemvParams g = gemv_base(ly.down_w, nullptr, M, H, d.inter_local, H);
+      g.x = mh.act;
+      g.ldx = d.inter_local;
+      g.comm = comm;
+      g.out_seq = SeqRef{uint32_t(2 * l + 2), nsite, 0u};
+      g.out_chan = chan;
+      MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
+      nprod = grid_down;
+    }
+  }
+
+  // final norm + LM head, consuming site 2L. With last_only, only the last
+  // chunk computes logits, and only for the last token of each batch row.
+  if (a.last_only && !last_chunk) return MTPB_OK;
+  {
+    const int rows = a.last_only ? a.B : M;
+    GemvParams g = gemv_base(d.lm_head, nullptr, rows, vloc, H, vloc);
+    const bool direct = fused_x && rows == M;
+    MTPB_TRY(prepare_input(g, uint32_t(2 * L), d.final_norm, direct));
+    if (!direct && a.last_only) {
+      g.x = static_cast<const char*>(mh.xn) + size_t(tc - 1) * H * sizeof(T);
+      g.ldx = tc * H;
+    }
+    g.y = a.logits ? a.logits : mh.logits;
+    g.ldy = vloc;
+    if (!a.last_only && chunked) {
+      g.tpr = tc;
+      g.out_T = a.T;
+      g.out_t0 = t0;
+    }
+    if (a.decode) {
+      g.best = mh.best;
+      g.vocab_start = uint32_t(d.vocab_start);
+      g.nan_wins = comm.world == 1 ? 1 : 0;
+      MTPB_TRY(gemv_dispatch<kEpiArgmax>(d.dtype, g, st));
+    } else {
+      if (!a.logits) return fail(MTPB_ERR_INVALID, "forward: logits output required");
+      MTPB_TRY(gemv_dispatch<kEpiStore>(d.dtype, g, st));
+    }
+  }
+
+  if (a.decode) {
+    ArgmaxFinishParams f;
+    std::memset(&f, 0, sizeof(f));
+    f.best = mh.best;
+    f.M = a.B;
+    f.comm = comm;
+    f.chan = chan;
+    f.seq = SeqRef{uint32_t(2 * L + 1), nsite, 0u};
+    f.tok_out = a.tok_out;
+    f.out_ids = a.out_ids;
+    f.ld_out = a.ld_out;
+    f.pos_ptr = a.pos_ptr;
+    MTPB_TRY(launch(argmax_finish_kernel, dim3(1), dim3(64), 0, st, f));
+  }
+  return MTPB_OK;
+}
+
+template <typename T>
+int model_forward_t(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
+  const mtpb_model_desc& d = mh.d;
+  const Comm& comm = mh.comm->dev;
+  if (a.cap > 0 && !a.pos_ptr && a.cache_len + a.T > a.cap) return fail(MTPB_ERR_INVALID, "KV cache overflow");
+  const size_t row_bytes = size_t(a.B) * d.hidden * sizeof(T);
+  if (row_bytes > comm.slot_bytes)
+    return fail(MTPB_ERR_INVALID, "forward: batch x hidden exceeds the communicator slot");
+  if (a.decode && (a.T != 1 || a.B > 64)) return fail(MTPB_ERR_INVALID, "decode step: T == 1 and B <= 64");
+  const int tc = int(std::min<size_t>(size_t(a.T), comm.slot_bytes / row_bytes));
+  MTPB_TRY(model_reserve(mh, a.B * tc, st));
+  for (int t0 = 0; t0 < a.T; t0 += tc) {
+    const int n = std::min(tc, a.T - t0);
+    MTPB_TRY(model_chunk_t<T>(mh, a, t0, n, t0 + n == a.T, st));
+  }
+  return MTPB_OK;
+}
+
+int model_forward(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
+  if (mh.d.dtype == MTPB_BF16) return model_forward_t<bf16>(mh, a, st);
+  if (mh.d.dtype == MTPB_F32) return model_forward_t<float>(mh, a, st);
+  return fail(MTPB_ERR_INVALID, "unsupported dtype");
+}
+
+}  // namespace
+
+// =====================================================================
+// extern "C"
+// =====================================================================
+extern "C" {
+
+const char* mtpb_last_error(void) { return g_err.c_str(); }
+int mtpb_version(void) { return 1; }
+int mtpb_set_pdl(int enable) {
+  g_pdl = enable != 0;
+  return MTPB_OK;
+}
+int mtpb_set_prefetch_cap(uint32_t bytes) {
+  g_prefetch_cap = bytes;
+  return MTPB_OK;
+}
+
+int mtpb_comm_create(int rank, int world, uint64_t slot_bytes, void** out) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return fail(MTPB_ERR_INVALID, "comm: need 1 <= world <= 8 and 0 <= rank < world");
+  if (slot_bytes % 256 != 0 || slot_bytes == 0) return fail(MTPB_ERR_INVALID, "comm: slot_bytes must be a positive multiple of 256");
+  auto* c = new CommHost();
+  std::memset(&c->dev, 0, sizeof(c->dev));
+  c->dev.rank = rank;
+  c->dev.world = world;
+  c->dev.slot_bytes = slot_bytes;
+  c->dev.timeout_ns = 5ull * 1000 * 1000 * 1000;
+  cudaGetDevice(&c->device);
+  const size_t bytes = Comm::buffer_bytes(slot_bytes, world);
+  cudaError_t e = cudaMalloc(&c->local, bytes);
+  if (e != cudaSuccess) {
+    delete c;
+    return fail_cuda(e, "cudaMalloc(comm buffer)");
+  }
+  e = cudaMemset(c->local, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(c->local);
+    delete c;
+    return fail_cuda(e, "cudaMemset(comm buffer)");
+  }
+  c->dev.base[rank] = static_cast<char*>(c->local);
+  c->open = world == 1;
+  *out = c;
+  return MTPB_OK;
+}
+
+int mtpb_comm_ipc_handle(void* comm, void* handle_out) {
+  if (!comm || !handle_out) return fail(MTPB_ERR_INVALID, "comm_ipc_handle: null argument");
+  auto* c = static_cast<CommHost*>(comm);
+  cudaIpcMemHandle_t h;
+  MTPB_CUDA(cudaIpcGetMemHandle(&h, c->local));
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  std::memcpy(handle_out, &h, 64);
+  return MTPB_OK;
+}
+
+int mtpb_comm_open(void* comm, const void* handles) {
+  if (!comm || !handles) return fail(MTPB_ERR_INVALID, "comm_open: null argument");
+  auto* c = static_cast<CommHost*>(comm);
+  if (c->open) return MTPB_OK;
+  for (int r = 0; r < c->dev.world; ++r) {
+    if (r == c->dev.rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + 64 * r, 64);
+    void* p = nullptr;
+    MTPB_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    c->mapped[r] = p;
+    c->dev.base[r] = static_cast<char*>(p);
+  }
+  c->open = true;
+  return MTPB_OK;
+}
+
+int mtpb_comm_destroy(void* comm) {
+  if (!comm) return MTPB_OK;
+  auto* c = static_cast<CommHost*>(comm);
+  for (int r = 0; r < kMaxRanks; ++r)
+    if (c->mapped[r]) cudaIpcCloseMemHandle(c->mapped[r]);
+  cudaFree(c->local);
+  delete c;
+  return MTPB_OK;
+}
+
+int mtpb_comm_set_timeout(void* comm, uint64_t ns) {
+  if (!comm) return fail(MTPB_ERR_INVALID, "comm_set_timeout: null comm");
+  static_cast<CommHost*>(comm)->dev.timeout_ns = ns;
+  return MTPB_OK;
+}
+
+int mtpb_comm_status(void* comm, uint32_t* out) {
+  CommHost* c = as_comm(comm);
+  if (!c || !out) return fail(MTPB_ERR_INVALID, "comm_status: null argument");
+  MTPB_CUDA(cudaDeviceSynchronize());
+  MTPB_CUDA(cudaMemcpy(out, c->dev.ctl() + kCtlStatus, 4, cudaMemcpyDeviceToHost));
+  return MTPB_OK;
+}
+
+int mtpb_comm_clear_status(void* comm) {
+  CommHost* c = as_comm(comm);
+  if (!c) return fail(MTPB_ERR_INVALID, "comm_clear_status: no communicator");
+  MTPB_CUDA(cudaMemset(c->dev.ctl() + kCtlStatus, 0, 4));
+  return MTPB_OK;
+}
+
+int* mtpb_comm_pos_ptr(void* comm) {
+  CommHost* c = as_comm(comm);
+  return c ? reinterpret_cast<int*>(c->dev.ctl() + kCtlPos) : nullptr;
+}
+
+int mtpb_comm_set_pos(void* comm, int pos, void* stream) {
+  CommHost* c = as_comm(comm);
+  if (!c) return fail(MTPB_ERR_INVALID, "comm_set_pos: no communicator");
+  int* p = reinterpret_cast<int*>(c->dev.ctl() + kCtlPos);
+  return launch(set_i32_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream), SetI32{p, pos});
+}
+
+uint64_t mtpb_comm_slot_bytes(void* comm) {
+  CommHost* c = as_comm(comm);
+  return c ? c->dev.slot_bytes : 0;
+}
+
+int mtpb_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int M, int N,
+                int K, int dtype, void* stream) {
+  GemvParams g = gemv_base(w, bias, M, N, K, N);
+  g.x = x;
+  g.ldx = ldx;
+  g.y = y;
+  g.ldy = ldy;
+  g.comm = as_comm(nullptr)->dev;
+  return gemv_dispatch<kEpiStore>(dtype, g, static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_linear_swiglu(const void* x, int ldx, const void* w, void* act, int ldact, int M, int I, int K,
+                       int dtype, void* stream) {
+  GemvParams g = gemv_base(w, nullptr, M, 2 * I, K, I);
+  g.x = x;
+  g.ldx = ldx;
+  g.y = act;
+  g.ldy = ldact;
+  g.comm = as_comm(nullptr)->dev;
+  return gemv_dispatch<kEpiSwiglu>(dtype, g, static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_qkv_rope(const void* x, int ldx, const void* w, const void* bias, void* q_out, void* k_cache,
+                  void* v_cache, int B, int T, int hq, int hkv, int hd, int K, int cap, int cache_len,
+                  const int64_t* rope_pos, const float* cos_tab, const float* sin_tab, int rope_len,
+                  int dtype, void* comm, void* stream) {
+  if (hd % 2 != 0) return fail(MTPB_ERR_INVALID, "qkv_rope: odd head_dim");
+  if (cache_len + T > cap) return fail(MTPB_ERR_INVALID, "KV cache overflow");
+  const int N = (hq + 2 * hkv) * hd;
+  GemvParams g = gemv_base(w, bias, B * T, N, K, N / 2);
+  g.x = x;
+  g.ldx = ldx;
+  g.y = q_out;
+  g.ldy = hq * hd;
+  g.comm = as_comm(comm)->dev;
+  g.cos_tab = cos_tab;
+  g.sin_tab = sin_tab;
+  g.rope_len = rope_len;
+  g.hd = hd;
+  g.hq = hq;
+  g.hkv = hkv;
+  g.k_cache = k_cache;
+  g.v_cache = v_cache;
+  g.kv_cap = cap;
+  g.tpr = T;
+  g.pos_base = cache_len;
+  g.rope_pos = reinterpret_cast<const long long*>(rope_pos);
+  return gemv_dispatch<kEpiRope>(dtype, g, static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_attention(const void* q, const void* k_cache, const void* v_cache, void* out, int B, int T, int hq,
+                   int hkv, int hd, int cap, int cache_len, int dtype, void* comm, void* stream) {
+  if (cache_len + T > cap) return fail(MTPB_ERR_INVALID, "attention: cache_len + T exceeds the cache capacity");
+  return attn_run(dtype, q, k_cache, v_cache, out, B, T, hq, hkv, hd, cap, nullptr, cache_len,
+                  standalone_attn_scratch(), as_comm(comm)->dev.status(), static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_rmsnorm(const void* x, const void* w, void* y, int rows, int H, float eps, int dtype, void* stream) {
+  if (rows <= 0 || H <= 0) return fail(MTPB_ERR_INVALID, "rmsnorm: empty shape");
+  const int grid = std::min(rows, sm_count() * 4);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  if (dtype == MTPB_BF16) {
+    MTPB_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<bf16>, x, w, y, rows, H, eps));
+  } else if (dtype == MTPB_F32) {
+    MTPB_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<float>, x, w, y, rows, H, eps));
+  } else {
+    return fail(MTPB_ERR_INVALID, "unsupported dtype");
+  }
+  return MTPB_OK;
+}
+
+int mtpb_allreduce_residual_rmsnorm(void* comm, const void* partial, const void* residual, const void* gain,
+                                    const void* bias, void* out_res, void* out_norm, int rows, int H, float eps,
+                                    int dtype, void* stream) {
+  CommHost* c = as_comm(comm);
+  if (!c || !c->open) return fail(MTPB_ERR_INVALID, "allreduce: communicator not open");
+  if (rows <= 0 || H <= 0) return fail(MTPB_ERR_INVALID, "allreduce: empty shape");
+  if ((out_norm == nullptr) != (gain == nullptr)) return fail(MTPB_ERR_INVALID, "allreduce: gain and out_norm go together");
+  ArNormParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.partial = partial;
+  p.residual = residual;
+  p.gain = gain;
+  p.bias = bias;
+  p.out_res = out_res;
+  p.out_norm = out_norm;
+  p.rows = rows;
+  p.H = H;
+  p.eps = eps;
+  p.comm = c->dev;
+  p.chan = 1;
+  const int VE = vec_elems(dtype);
+  if (H % VE == 0 && (!aligned16(partial))) return fail(MTPB_ERR_INVALID, "allreduce: partial must be 16-byte aligned");
+  return ar_norm_run(dtype, p, static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_allreduce(void* comm, void* t, int rows, int H, int dtype, void* stream) {
+  return mtpb_allreduce_residual_rmsnorm(comm, t, nullptr, nullptr, nullptr, t, nullptr, rows, H, 0.f, dtype,
+                                         stream);
+}
+
+int mtpb_embedding(void* comm, const int64_t* ids, const void* table, void* out, int M, int H, int64_t vstart,
+                   int64_t vend, int64_t vocab, int dtype, void* stream) {
+  CommHost* c = as_comm(comm);
+  if (!c || !c->open) return fail(MTPB_ERR_INVALID, "embedding: communicator not open");
+  if (M <= 0 || H <= 0) return fail(MTPB_ERR_INVALID, "embedding: empty shape");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int VE = vec_elems(dtype);
+  if (H % VE == 0 && (!aligned16(table) || !aligned16(out)))
+    return fail(MTPB_ERR_INVALID, "embedding: table and out must be 16-byte aligned");
+  EmbedParams e;
+  std::memset(&e, 0, sizeof(e));
+  e.ids = reinterpret_cast<const long long*>(ids);
+  e.table = table;
+  e.M = M;
+  e.H = H;
+  e.vstart = vstart;
+  e.vend = vend;
+  e.vtotal = vocab;
+  e.comm = c->dev;
+  if (c->dev.world == 1) {
+    e.out = out;
+    return embed_run(dtype, e, std::min(M, 1024), st);
+  }
+  if (size_t(M) * H * dsize(dtype) > c->dev.slot_bytes)
+    return fail(MTPB_ERR_INVALID, "embedding: rows x hidden exceed the communicator slot");
+  // masked lookup into a local partial, then the one-shot reduce (channel 1)
+  e.out = out;
+  Comm solo = c->dev;
+  solo.world = 1;
+  e.comm = solo;
+  MTPB_TRY(embed_run(dtype, e, std::min(M, 1024), st));
+  return mtpb_allreduce(comm, out, M, H, dtype, stream);
+}
+
+int mtpb_argmax(void* comm, const void* logits, int M, int V_local, int64_t ld, int64_t vstart, int64_t* ids_out,
+                int64_t* scratch, int dtype, void* stream) {
+  CommHost* c = as_comm(comm);
+  if (!c || !c->open) return fail(MTPB_ERR_INVALID, "argmax: communicator not open");
+  if (M <= 0 || M > 64) return fail(MTPB_ERR_INVALID, "argmax: need 1 <= M <= 64 rows");
+  if (V_local <= 0) return fail(MTPB_ERR_INVALID, "argmax: empty vocab shard");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ArgmaxRowsParams a;
+  a.logits = logits;
+  a.M = M;
+  a.V = V_local;
+  a.ld = ld;
+  a.vstart = uint32_t(vstart);
+  a.nan_wins = c->dev.world == 1 ? 1 : 0;
+  a.part = reinterpret_cast<long long*>(scratch);
+  MTPB_TRY(argmax_rows_run(dtype, a, st));
+  ArgmaxFinishParams f;
+  std::memset(&f, 0, sizeof(f));
+  f.part = reinterpret_cast<const long long*>(scratch);
+  f.nsplit = argmax_splits(V_local);
+  f.M = M;
+  f.comm = c->dev;
+  f.chan = 1;
+  f.use_coll_counter = 1;
+  f.tok_out = reinterpret_cast<long long*>(ids_out);
+  return launch(argmax_finish_kernel, dim3(1), dim3(64), 0, st, f);
+}
+
+int mtpb_model_create(const mtpb_model_desc* desc, void* comm, void** out) {
+  if (!desc || !out) return fail(MTPB_ERR_INVALID, "model_create: null argument");
+  CommHost* c = as_comm(comm);
+  if (!c || !c->open) return fail(MTPB_ERR_INVALID, "model_create: communicator not open");
+  const mtpb_model_desc& d = *desc;
+  if (d.n_layers <= 0 || d.hidden <= 0 || d.head_dim <= 0 || d.hq_local <= 0 || d.hkv_local <= 0)
+    return fail(MTPB_ERR_INVALID, "model_create: bad dimensions");
+  if (d.hq_local % d.hkv_local != 0) return fail(MTPB_ERR_INVALID, "model_create: hq_local % hkv_local != 0");
+  if (2 * d.n_layers + 2 > 4096) return fail(MTPB_ERR_INVALID, "model_create: too many layers");
+  if (d.vocab_end - d.vocab_start <= 0 || d.vocab_size >= (int64_t(1) << 32))
+    return fail(MTPB_ERR_INVALID, "model_create: bad vocab range");
+  auto* mh = new ModelHost();
+  mh->d = d;
+  mh->layers.resize(d.n_layers);
+  std::memset(mh->layers.data(), 0, sizeof(mtpb_layer_desc) * d.n_layers);
+  mh->comm = c;
+  *out = mh;
+  return MTPB_OK;
+}
+
+int mtpb_model_set_layer(void* model, int layer, const mtpb_layer_desc* desc) {
+  if (!model || !desc) return fail(MTPB_ERR_INVALID, "model_set_layer: null argument");
+  auto* mh = static_cast<ModelHost*>(model);
+  if (layer < 0 || layer >= mh->d.n_layers) return fail(MTPB_ERR_INVALID, "model_set_layer: layer out of range");
+  mh->layers[layer] = *desc;
+  return MTPB_OK;
+}
+
+int mtpb_model_reserve(void* model, int max_rows, int max_cap) {
+  if (!model) return fail(MTPB_ERR_INVALID, "model_reserve: null model");
+  auto* mh = static_cast<ModelHost*>(model);
+  MTPB_TRY(model_reserve(*mh, max_rows, nullptr));
+  // attention split scratch for decode rows (T = 1) at this capacity
+  const int G = mh->d.hq_local / mh->d.hkv_local;
+  int cc = 0;
+  const int M = std::min(max_rows, 64);
+  const int ns = attn_choose_splits(M, mh->d.hkv_local, G, max_cap, mh->d.head_dim, &cc);
+  if (ns > 1) {
+    AttnScratch& s = mh->ascr;
+    const size_t need_o = size_t(M) * mh->d.hq_local * ns * mh->d.head_dim;
+    const size_t need_ml = size_t(M) * mh->d.hq_local * ns * 2, need_c = size_t(M) * mh->d.hkv_local;
+    if (need_o > s.o_elems || need_ml > s.ml_elems || need_c > s.ctr_elems) {
+      cudaFree(s.part_o);
+      cudaFree(s.part_ml);
+      cudaFree(s.counters);
+      MTPB_CUDA(cudaMalloc(&s.part_o, need_o * 4));
+      MTPB_CUDA(cudaMalloc(&s.part_ml, need_ml * 4));
+      MTPB_CUDA(cudaMalloc(&s.counters, need_c * 4));
+      MTPB_CUDA(cudaMemset(s.counters, 0, need_c * 4));
+      s.o_elems = need_o;
+      s.ml_elems = need_ml;
+      s.ctr_elems = need_c;
+    }
+  }
+  return MTPB_OK;
+}
+
+int mtpb_model_destroy(void* model) {
+  if (!model) return MTPB_OK;
+  auto* mh = static_cast<ModelHost*>(model);
+  cudaFree(mh->scratch);
+  cudaFree(mh->ascr.part_o);
+  cudaFree(mh->ascr.part_ml);
+  cudaFree(mh->ascr.counters);
+  delete mh;
+  return MTPB_OK;
+}
+
+int mtpb_model_forward(void* model, const int64_t* ids, int B, int T, const int64_t* rope_pos, int cache_len,
+                       void* const* k_caches, void* const* v_caches, int cap, void* logits, int last_only,
+                       void* stream) {
+  if (!model || !ids || !k_caches || !v_caches) return fail(MTPB_ERR_INVALID, "model_forward: null argument");
+  if (B <= 0 || T <= 0) return fail(MTPB_ERR_INVALID, "model_forward: empty batch");
+  auto* mh = static_cast<ModelHost*>(model);
+  FwdArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.ids = reinterpret_cast<const long long*>(ids);
+  a.B = B;
+  a.T = T;
+  a.rope_pos = reinterpret_cast<const long long*>(rope_pos);
+  a.cache_len = cache_len;
+  a.kc = k_caches;
+  a.vc = v_caches;
+  a.cap = cap;
+  a.logits = logits;
+  a.last_only = last_only;
+  return model_forward(*mh, a, static_cast<cudaStream_t>(stream));
+}
+
+int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_caches, void* const* v_caches, int cap,
+                           int64_t* out_ids, int ld_out, void* logits, void* stream) {
+  if (!model || !tok || !k_caches || !v_caches) return fail(MTPB_ERR_INVALID, "model_decode_step: null argument");
+  if (B <= 0 || B > 64) return fail(MTPB_ERR_INVALID, "model_decode_step: need 1 <= B <= 64");
+  auto* mh = static_cast<ModelHost*>(model);
+  FwdArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.ids = reinterpret_cast<const long long*>(tok);
+  a.B = B;
+  a.T = 1;
+  a.pos_ptr = reinterpret_cast<int*>(mh->comm->dev.ctl() + kCtlPos);
+  a.kc = k_caches;
+  a.vc = v_caches;
+  a.cap = cap;
+  a.logits = logits;
+  a.last_only = 0;
+  a.decode = true;
+  a.tok_out = reinterpret_cast<long long*>(tok);
+  a.out_ids = reinterpret_cast<long long*>(out_ids);
+  a.ld_out = ld_out;
+  return model_forward(*mh, a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

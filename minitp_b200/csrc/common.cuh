@@ -1,0 +1,224 @@
+// Shared device helpers for the minitp_b200 kernels (sm_100a only).
+//
+// * 16-byte vector loads/stores and bf16 <-> fp32 conversion.
+// * Programmatic dependent launch (PDL): every kernel calls pdl_launch() and
+//   pdl_wait() unconditionally in every CTA, so "grid N completed" implies
+//   "grids before N completed" along the whole stream.
+// * System-scope release/acquire flags for NVLink peer signalling, with
+//   bounded waits: a wait that runs past its budget records an error in the
+//   status word and returns; it never spins forever.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifndef __CUDA_ARCH__
+#define MTPB_HOST_ONLY 1
+#endif
+
+namespace mtpb {
+
+constexpr int kMaxRanks = 8;
+
+// ---------------------------------------------------------------- status
+// Error bits recorded in a device status word (read by the host after a step).
+enum : uint32_t {
+  kStatusOk = 0,
+  kStatusTimeout = 1u << 0,      // a bounded wait on peer flags ran out
+  kStatusBadPosition = 1u << 1,  // a position >= KV capacity or RoPE table size
+  kStatusBadToken = 1u << 2,     // a token id outside [0, vocab)
+};
+
+// ---------------------------------------------------------------- types
+using bf16 = __nv_bfloat16;
+
+template <typename T> struct VecTraits;
+template <> struct VecTraits<float> { static constexpr int kElems = 4; };
+template <> struct VecTraits<bf16> { static constexpr int kElems = 8; };
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(bf16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+
+// Round through the storage type: the value a tensor of type T would hold.
+template <typename T> __device__ __forceinline__ float round_t(float v) { return to_f(from_f<T>(v)); }
+
+// Unpack one 16-byte vector into fp32 lanes.
+__device__ __forceinline__ void unpack(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ void unpack(const uint4& u, float (&f)[4]) {
+  f[0] = __uint_as_float(u.x);
+  f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z);
+  f[3] = __uint_as_float(u.w);
+}
+
+// Streaming 16-byte load of read-only data (weights): no L1 allocation.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// 16-byte load through L1 (activations reused by every warp of the CTA).
+__device__ __forceinline__ uint4 ld_vec(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// ---------------------------------------------------------------- PDL
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetch a byte range into L2 from one thread, in pieces of at most 1 MiB.
+__device__ __forceinline__ void prefetch_range_l2(const void* base, size_t bytes) {
+  const char* p = static_cast<const char*>(base);
+  uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  uintptr_t lo = (a + 15) & ~uintptr_t(15);
+  uintptr_t hi = (a + bytes) & ~uintptr_t(15);
+  while (lo < hi) {
+    const uintptr_t left = hi - lo, cap = uintptr_t(1) << 20;
+    const uint32_t n = static_cast<uint32_t>(left < cap ? left : cap);
+    prefetch_l2(reinterpret_cast<const void*>(lo), n);
+    lo += n;
+  }
+}
+
+// ---------------------------------------------------------------- timers, flags
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+
+// true when flag value `v` has reached sequence number `seq` (wrap-safe).
+__device__ __forceinline__ bool seq_reached(uint32_t v, uint32_t seq) {
+  return static_cast<int32_t>(v - seq) >= 0;
+}
+
+// Block-wide bounded wait until flags[i] >= seq for every i in [0, n).
+// Every thread of the block must call it. Returns false (after recording
+// kStatusTimeout in *status) when the budget runs out or when another wait
+// already failed; the caller then skips its work and returns.
+__device__ __forceinline__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t seq,
+                                                 uint32_t* status, uint64_t timeout_ns) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  bool ok = true;
+  uint64_t t0 = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    uint32_t spins = 0;
+    while (!seq_reached(ld_acquire_sys(flags + i), seq)) {
+      if ((++spins & 63u) == 0) {
+        if (t0 == 0) t0 = global_ns();
+        if (ld_volatile_u32(status) != 0 || global_ns() - t0 > timeout_ns) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) break;
+  }
+  if (!ok) {
+    atomicOr(status, kStatusTimeout);
+    s_ok = 0;
+  }
+  __syncthreads();
+  bool res = s_ok != 0;
+  __syncthreads();
+  return res;
+}
+
+// ---------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum over the block; result valid in every thread. `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nwarps; ++i) t += red[i];  // fixed order: deterministic
+  return t;
+}
+
+// ---------------------------------------------------------------- greedy argmax keys
+// Packed argmax key, order-preserving over (value, -id):
+//   key32 = bits(v) for v >= +0, (~bits(v) & 0xFFFFFFFF) - 2^31 for v < 0,
+//   packed = (int64(key32) << 32) | (0xFFFFFFFF - id).
+// The larger packed value has the larger logit; equal logits favour the smaller id.
+// -0.0 is normalised to +0.0. NaN handling depends on `nan_wins`: the TP=1
+// path follows torch.argmax (NaN beats everything, first NaN wins), the TP>1
+// path maps NaN to -inf so a NaN logit cannot win.
+__device__ __forceinline__ long long argmax_pack(float v, uint32_t id, bool nan_wins) {
+  int64_t key;
+  if (v != v) {
+    if (nan_wins) {
+      key = 0x7FFFFFFFll;
+    } else {
+      v = -__int_as_float(0x7f800000);
+      uint32_t bits = __float_as_uint(v);
+      key = static_cast<int64_t>(~bits & 0xFFFFFFFFu) - 0x80000000ll;
+    }
+  } else {
+    if (v == 0.f) v = 0.f;
+    uint32_t bits = __float_as_uint(v);
+    key = bits < 0x80000000u ? static_cast<int64_t>(bits)
+                             : static_cast<int64_t>(~bits & 0xFFFFFFFFu) - 0x80000000ll;
+  }
+  return static_cast<long long>((static_cast<uint64_t>(key) << 32) |
+                                static_cast<uint64_t>(0xFFFFFFFFu - id));
+}
+__device__ __forceinline__ long long argmax_id(long long packed) {
+  return static_cast<long long>(0xFFFFFFFFull - (static_cast<uint64_t>(packed) & 0xFFFFFFFFull));
+}
+constexpr long long kArgmaxEmpty = (-0x7FFFFFFFFFFFFFFFll - 1);
+
+__device__ __forceinline__ long long warp_max_ll(long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
+  }
+  return v;
+}
+
+}  // namespace mtpb

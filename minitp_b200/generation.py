@@ -1,0 +1,199 @@
+"""Greedy generation over the per-rank KV cache (reference: minitp/generation.py).
+
+``GenerationState`` keeps the reference API (prefill / select_next / append /
+decode_step, ``out_ids``, ``positions_buf``, ``cursor``). ``generate_greedy``
+with a fixed length (``early_stop=False``, or no EOS id) runs the decode loop
+as replays of one CUDA graph. The graph holds one captured
+``mtpb_model_decode_step``: the embedding of the current token, all layers,
+the LM head with the packed-key argmax, the NVLink exchange of the winners,
+and the write of the token to ``out_ids[:, pos + 1]`` with the position
+advance. Token, position and collective sequence numbers live on the
+device, so replays need no host input and no synchronisation.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from minitp_b200 import _lib, ops
+from minitp_b200.distributed import all_gather
+from minitp_b200.kv_cache import KVCache
+from minitp_b200.layer import TPQwen2ForCausalLM
+
+
+def _kv_heads_local(model: TPQwen2ForCausalLM) -> int:
+    return model.model.layers[0].self_attn.kv_heads_local
+
+
+def make_kv_cache(model: TPQwen2ForCausalLM, batch_size: int, max_seq_len: int, init: str = "empty") -> KVCache:
+    """Reference: generation.py:36-51."""
+    p = next(model.parameters())
+    return KVCache(model.cfg.num_hidden_layers, batch_size, _kv_heads_local(model), model.cfg.head_dim,
+                   max_seq_len, p.dtype, p.device, init=init)
+
+
+def select_token(model: TPQwen2ForCausalLM, logits: torch.Tensor, distributed_argmax: bool = True) -> torch.Tensor:
+    """Greedy pick from local logits ``[B, T, V_local]``; identical on every rank (generation.py:54-67)."""
+    if distributed_argmax:
+        return model.lm_head.distributed_argmax(logits[:, -1]).squeeze(-1)
+    if model.ctx.tp_size == 1:
+        return ops.argmax(logits[:, -1], 0, None).squeeze(-1)
+    full = torch.empty(*logits.shape[:-2], model.cfg.vocab_size, dtype=logits.dtype, device=logits.device)
+    all_gather(full, logits[:, -1].contiguous(), model.ctx.process_group)
+    return ops.argmax(full, 0, None).squeeze(-1)
+
+
+class GenerationState:
+    """KV cache + positions buffer + output buffer (reference generation.py:70-130)."""
+
+    def __init__(
+        self,
+        model: TPQwen2ForCausalLM,
+        input_ids: torch.Tensor,
+        max_new_tokens: int,
+        kv: KVCache | None = None,
+        distributed_argmax: bool = True,
+        kv_init: str = "empty",
+    ) -> None:
+        self.model = model
+        self.distributed_argmax = distributed_argmax
+        b, t = input_ids.shape
+        self.batch = b
+        self.prompt_len = t
+        self.max_new_tokens = max_new_tokens
+        self.total = t + max_new_tokens
+        self.kv = kv if kv is not None else make_kv_cache(model, b, self.total, init=kv_init)
+        device = input_ids.device
+        self.out_ids = torch.empty(b, self.total, dtype=torch.long, device=device)
+        self.out_ids[:, :t] = input_ids
+        self.positions_buf = torch.arange(self.total, device=device)
+        self.cursor = t
+        self.finished: torch.Tensor | None = None
+        self.eos = -1
+        self._graph: torch.cuda.CUDAGraph | None = None
+        self._tok: torch.Tensor | None = None
+
+    def prefill(self, last_only: bool = False) -> torch.Tensor:
+        positions = self.positions_buf[: self.prompt_len]
+        return self.model(self.out_ids[:, : self.prompt_len], positions=positions, kv_cache=self.kv,
+                          last_only=last_only)
+
+    def select_next(self, logits: torch.Tensor) -> torch.Tensor:
+        return select_token(self.model, logits, self.distributed_argmax)
+
+    def append(self, tok: torch.Tensor) -> torch.Tensor:
+        self.out_ids[:, self.cursor] = tok
+        pos = self.positions_buf[self.cursor]
+        self.cursor += 1
+        return pos
+
+    def decode_step(self, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        return self.model(tok.unsqueeze(-1), positions=pos.unsqueeze(-1), kv_cache=self.kv)
+
+    # ------------------------------------------------------------------
+    # device-resident decode (graph replays)
+    # ------------------------------------------------------------------
+    def _step_args(self):
+        kp, vp = self.kv.pointer_arrays()
+        return (self.model.native(), self._tok.data_ptr(), self.batch, kp, vp, self.kv.max_seq_len,
+                self.out_ids.data_ptr(), self.total, None)
+
+    def start_device_decode(self, tok: torch.Tensor) -> None:
+        """Seed the device loop with the token just appended at ``cursor - 1``."""
+        if self.batch > 64:
+            raise ValueError("device decode supports at most 64 rows")
+        comm = self.model.ctx.comm()
+        self._tok = tok.to(torch.int64).contiguous().clone()
+        _lib.call("mtpb_comm_set_pos", comm.handle, self.cursor - 1, _lib.stream_ptr(self._tok.device))
+        h = self.model.native()
+        _lib.call("mtpb_model_reserve", h, self.batch, self.kv.max_seq_len)
+
+    def device_step(self) -> None:
+        """One decode step + greedy selection, all on the device (no graph)."""
+        self.kv.check_room(1)
+        _lib.call("mtpb_model_decode_step", *self._step_args(), _lib.stream_ptr(self._tok.device))
+        self.kv.advance(1)
+        self.cursor += 1
+
+    def capture(self) -> None:
+        """Capture one device decode step into a CUDA graph."""
+        g = torch.cuda.CUDAGraph()
+        args = self._step_args()
+        with torch.cuda.graph(g):
+            _lib.call("mtpb_model_decode_step", *args, _lib.stream_ptr(self._tok.device))
+        self._graph = g
+
+    def graph_step(self) -> None:
+        self.kv.check_room(1)
+        self._graph.replay()
+        self.kv.advance(1)
+        self.cursor += 1
+
+    def run_fixed(self, use_graph: bool = True) -> torch.Tensor:
+        """Fixed-length greedy generation (the reference loop with early_stop=False)."""
+        logits = self.prefill(last_only=True)
+        tok = self.select_next(logits)
+        self.append(tok)
+        steps = self.max_new_tokens - 1
+        if steps <= 0:
+            return self.out_ids
+        self.start_device_decode(tok)
+        self.device_step()  # first step eagerly: sets function attributes, validates the chain
+        if steps > 1:
+            if use_graph:
+                self.capture()
+                for _ in range(steps - 1):
+                    self.graph_step()
+            else:
+                for _ in range(steps - 1):
+                    self.device_step()
+        return self.out_ids
+
+    def release(self) -> None:
+        self._graph = None
+
+
+@torch.inference_mode()
+def generate_greedy(
+    model: TPQwen2ForCausalLM,
+    input_ids: torch.Tensor,
+    max_new_tokens: int,
+    eos_token_id: int | None = None,
+    distributed_argmax: bool = True,
+    early_stop: bool = True,
+    kv: KVCache | None = None,
+    kv_init: str = "empty",
+) -> torch.Tensor:
+    """Greedy decode (reference generation.py:133-171).
+
+    Returns ``[B, prompt + generated]``: trimmed at the first step where all
+    rows hit EOS when ``early_stop=True``; exactly prompt + max_new_tokens
+    columns otherwise.
+    """
+    state = GenerationState(model, input_ids, max_new_tokens, kv=kv, distributed_argmax=distributed_argmax,
+                            kv_init=kv_init)
+    b = input_ids.shape[0]
+    fixed = not (early_stop and eos_token_id is not None)
+    if fixed and distributed_argmax and b <= 64:
+        out = state.run_fixed(use_graph=True)
+        state.release()
+        return out if not early_stop else out[:, : state.cursor]
+    if early_stop and eos_token_id is not None:
+        state.eos = eos_token_id
+        state.finished = torch.zeros(b, dtype=torch.bool, device=input_ids.device)
+    logits = state.prefill(last_only=True)
+    eos_tok = torch.tensor(state.eos, device=input_ids.device)
+    for step in range(max_new_tokens):
+        tok = state.select_next(logits)
+        if state.finished is not None:
+            tok = torch.where(state.finished, eos_tok, tok)
+            state.finished = state.finished | (tok == state.eos)
+        pos = state.append(tok)
+        if state.finished is not None and bool(state.finished.all()):
+            break
+        if step + 1 < max_new_tokens:
+            logits = state.decode_step(tok, pos)
+    return state.out_ids[:, : state.cursor] if early_stop else state.out_ids
+
+
+__all__ = ["GenerationState", "generate_greedy", "make_kv_cache", "select_token"]

@@ -1,0 +1,158 @@
+"""End-to-end parity of the B200 model path against fixtures recorded from the reference.
+
+Tolerances come from the reference's own tests and the north star:
+* greedy token ids: bit-exact (fp32 runs are the binding token check),
+* fp32 logits: within 1e-4 relative (tests/test_qwen_tiny.py:119),
+* bf16 logits: within 0.5 absolute (tests/test_qwen_real.py:55).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import golden
+from minitp_b200 import config as mcfg
+
+pytestmark = pytest.mark.gpu
+
+DT = {"fp32": torch.float32, "bf16": torch.bfloat16}
+RUNS = {
+    "tiny": (mcfg.baseline_tiny, 1, 8, 16),
+    "q05b": (mcfg.qwen25_05b, 1, 128, 128),
+    "q05b_b4": (mcfg.qwen25_05b, 4, 32, 16),
+    "q7b_l2": (lambda: mcfg.qwen25_7b(num_layers=2), 1, 16, 8),
+}
+_MODELS: dict = {}
+
+
+def _model(name: str, dtype: str):
+    key = (name, dtype)
+    if key not in _MODELS:
+        from minitp_b200.distributed.context import context_for
+        from minitp_b200.weight_loader import load_synthetic_tp
+
+        _MODELS.clear()
+        torch.cuda.empty_cache()
+        cfg = RUNS[name][0]()
+        _MODELS[key] = load_synthetic_tp(cfg, context_for(1, "cuda"), dtype=DT[dtype], device=torch.device("cuda"))
+    return _MODELS[key]
+
+
+def _rel_err(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("name", ["tiny", "q05b", "q05b_b4", "q7b_l2"])
+def test_fp32_tokens_and_logits(lib, name):
+    from minitp_b200.generation import generate_greedy
+
+    g = golden(f"model_{name}_tp1_fp32.npz")
+    _, b, p, n = RUNS[name]
+    model = _model(name, "fp32")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    # prefill logits of the last position vs the reference
+    logits = model(ids, positions=torch.arange(p, device="cuda")).float().cpu().numpy()[:, -1]
+    assert _rel_err(logits, g["prefill_last_logits"]) < 1e-4
+    out = generate_greedy(model, ids, n, early_stop=False)
+    model.ctx.comm().raise_on_error()
+    got = out.cpu().numpy()
+    assert np.array_equal(got, g["tokens"]), f"first mismatch at {np.argwhere(got != g['tokens'])[:3].tolist()}"
+
+
+@pytest.mark.parametrize("name", ["tiny", "q05b", "q7b_l2"])
+def test_bf16_logits(lib, name):
+    g = golden(f"model_{name}_tp1_bf16.npz")
+    _, b, p, n = RUNS[name]
+    model = _model(name, "bf16")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    logits = model(ids, positions=torch.arange(p, device="cuda")).float().cpu().numpy()[:, -1]
+    assert np.abs(logits - g["prefill_last_logits"]).max() < 0.5
+
+
+def test_decode_logits_match_reference_step(lib):
+    """The logits of decode step 1, fed the reference's own tokens (fp32, 1e-4)."""
+    from minitp_b200.generation import GenerationState
+
+    g = golden("model_q05b_tp1_fp32.npz")
+    model = _model("q05b", "fp32")
+    toks = torch.from_numpy(g["tokens"]).cuda()
+    st = GenerationState(model, toks[:, :128], 128)
+    st.prefill()
+    st.append(toks[:, 128])
+    logits = st.decode_step(toks[:, 128], st.positions_buf[128])
+    assert _rel_err(logits.float().cpu().numpy()[:, -1], g["decode1_logits"]) < 1e-4
+
+
+def test_graph_path_equals_eager_path(lib):
+    """generate_greedy (device loop in a CUDA graph) == the eager GenerationState loop."""
+    from minitp_b200.generation import GenerationState, generate_greedy
+
+    model = _model("q05b", "bf16")
+    g = golden("model_q05b_tp1_bf16.npz")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    fast = generate_greedy(model, ids, 24, early_stop=False)
+    st = GenerationState(model, ids, 24)
+    logits = st.prefill()
+    for step in range(24):
+        tok = st.select_next(logits)
+        pos = st.append(tok)
+        if step + 1 < 24:
+            logits = st.decode_step(tok, pos)
+    assert torch.equal(fast, st.out_ids)
+
+
+def test_early_stop_and_eos(lib):
+    from minitp_b200.generation import generate_greedy
+
+    model = _model("q05b", "bf16")
+    g = golden("model_q05b_tp1_bf16.npz")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    fixed = generate_greedy(model, ids, 12, early_stop=False)
+    eos = int(fixed[0, 128 + 5])
+    stopped = generate_greedy(model, ids, 12, eos_token_id=eos, early_stop=True)
+    first = int((fixed[0, 128:] == eos).nonzero()[0])
+    assert stopped.shape[1] == 128 + first + 1
+    assert torch.equal(stopped, fixed[:, : stopped.shape[1]])
+
+
+def test_poisoned_cache_is_never_read(lib):
+    """Reference tests/test_kv_cache.py:41-120: NaN-poisoned K and V, write-before-read."""
+    from minitp_b200.generation import GenerationState, generate_greedy, make_kv_cache
+
+    model = _model("tiny", "fp32")
+    g = golden("model_tiny_tp1_fp32.npz")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    kv = make_kv_cache(model, 1, 24)
+    kv.poison()
+    out = generate_greedy(model, ids, 16, early_stop=False, kv=kv)
+    assert np.array_equal(out.cpu().numpy(), g["tokens"])
+    for buf in (*kv.k, *kv.v):
+        assert torch.isfinite(buf[:, :, :23]).all()
+        assert torch.isnan(buf[:, :, 24:]).all() if buf.shape[2] > 24 else True
+    kv2 = make_kv_cache(model, 1, 16)
+    kv2.poison()
+    st = GenerationState(model, ids, 4, kv=kv2)
+    logits = st.prefill()
+    tok = st.select_next(logits)
+    for _ in range(4):
+        pos = st.append(tok)
+        logits = st.decode_step(tok, pos)
+        tok = st.select_next(logits)
+    assert kv2.seq_len == 12
+    for buf in (*kv2.k, *kv2.v):
+        assert torch.isfinite(buf[:, :, :12]).all()
+        assert torch.isnan(buf[:, :, 12:]).all()
+
+
+def test_kv_overflow_raises(lib):
+    from minitp_b200.generation import make_kv_cache
+
+    model = _model("tiny", "fp32")
+    kv = make_kv_cache(model, 1, 6)
+    with pytest.raises(ValueError, match="overflow"):
+        model(torch.randint(3, 100, (1, 8), device="cuda"), kv_cache=kv)
+
+
+def test_status_clean_after_runs(lib):
+    for (name, dt), m in list(_MODELS.items()):
+        assert m.ctx.comm().status() == 0
