@@ -55,6 +55,9 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-pdl", action="store_true")
     p.add_argument("--out", default=None, help="also write the JSON line here")
+    p.add_argument("--workload", default="decode", choices=["decode", "fused_ar"],
+                   help="decode (default) or the fused AllReduce+residual+RMSNorm microbenchmark")
+    p.add_argument("--iters", type=int, default=10000, help="fused_ar: iterations per size")
     return p.parse_args(argv)
 
 
@@ -379,8 +382,97 @@ def run_b200(args, cfg, prompt_len, new_tokens):
     ctx.destroy()
 
 
+def run_fused_ar(args):
+    """Fused AllReduce + residual + RMSNorm vs NCCL all_reduce, [rows, 896] bf16.
+
+    Both are replayed from CUDA graphs of `chunk` back-to-back calls, so the
+    numbers are device time per call (max over ranks), not host launch time.
+    Prints one JSON line per size on rank 0.
+    """
+    import torch.distributed as dist
+
+    from minitp_b200 import ops
+    from minitp_b200.build import build
+    from minitp_b200.distributed.context import init_context
+    from minitp_b200.synthetic_cases import fused_ar_case
+
+    if int(os.environ.get("RANK", "0")) == 0:
+        build()
+    ctx = init_context(timeout_s=120.0)
+    world = ctx.tp_size
+    if world < 2:
+        if ctx.is_rank_zero:
+            print(json.dumps({"workload": "fused_ar", "skipped": "needs >= 2 GPUs"}))
+        return
+    dist.barrier()
+    comm = ctx.comm()
+    dev = ctx.device
+    results = []
+    chunk = 100
+    for rows in (1, 8, 64, 128, 512, 2048):
+        partials, residual, gain = fused_ar_case(rows, 896, world, seed=1000 + rows)
+        p = partials[ctx.tp_rank].to(dev)
+        r = residual.to(dev)
+        g = gain.to(dev)
+        out_res = torch.empty_like(p)
+        out_norm = torch.empty_like(p)
+        nccl_t = p.clone()
+        from minitp_b200 import _lib
+
+        def fused():
+            _lib.call("mtpb_allreduce_residual_rmsnorm", comm.handle, p.data_ptr(), r.data_ptr(), g.data_ptr(),
+                      None, out_res.data_ptr(), out_norm.data_ptr(), rows, 896, 1e-6, _lib.MTPB_BF16,
+                      _lib.stream_ptr(dev))
+
+        def nccl():
+            dist.all_reduce(nccl_t)
+
+        times = {}
+        for name, fn in (("fused", fused), ("nccl", nccl)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(chunk):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            reps = max(1, args.iters // chunk)
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            for _ in range(reps):
+                graph.replay()
+            e.record()
+            torch.cuda.synchronize()
+            us = s.elapsed_time(e) * 1e3 / (reps * chunk)
+            t = torch.tensor([us], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times[name] = t.item()
+            del graph
+        comm.raise_on_error()
+        m = rows * 896 * 2
+        line = {"workload": "fused_ar", "metric": "fused AR+residual+RMSNorm latency", "rows": rows,
+                "bytes": m, "tp": world, "unit": "us", "fused_us": round(times["fused"], 3),
+                "nccl_allreduce_us": round(times["nccl"], 3),
+                "ratio_fused_over_nccl": round(times["fused"] / times["nccl"], 3),
+                "fused_nvlink_send_gbs": round((world - 1) * m / (times["fused"] * 1e-6) / 1e9, 2),
+                "iters": (max(1, args.iters // chunk)) * chunk}
+        results.append(line)
+        if ctx.is_rank_zero:
+            print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ctx.destroy()
+
+
 def main(argv=None):
     args = parse_args(argv)
+    if args.workload == "fused_ar":
+        run_fused_ar(args)
+        return
     cfg, prompt_len, new_tokens = workload(args)
     if args.impl == "reference":
         run_reference(args, cfg, prompt_len, new_tokens)

@@ -43,6 +43,9 @@ int mtpb_set_pdl(int enable);
 /* Upper bound of weight bytes each GEMV CTA prefetches into L2 before it
  * waits for the previous kernel (default 4 MiB; 0 disables the prefetch). */
 int mtpb_set_prefetch_cap(uint32_t bytes);
+/* GEMV grid size in CTAs per SM (default 2, range [1, 8]); applies to later launches
+ * and to graph captures made after the call. */
+int mtpb_set_gemv_ctas_per_sm(int n);
 
 /* ------------------------------------------------------- communicator
  * Peer-memory communicator over NVLink (one per rank; TP group == world).

@@ -18,6 +18,17 @@ import torch.distributed as dist
 from minitp_b200 import _lib
 
 
+def exchange_handles(process_group, mine: bytes, world: int) -> bytes:
+    """All ranks' 64-byte IPC handles concatenated in rank order (one collective)."""
+    if len(mine) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    handles: list = [None] * world
+    dist.all_gather_object(handles, bytes(mine), group=process_group)
+    if any(h is None or len(h) != 64 for h in handles):
+        raise RuntimeError("IPC handle exchange returned a malformed handle")
+    return b"".join(handles)
+
+
 class NvlinkComm:
     """Owns a ``mtpb_comm`` handle (see include/minitp_b200.h)."""
 
@@ -39,9 +50,8 @@ class NvlinkComm:
                     raise ValueError("tp_size > 1 needs a process group to exchange IPC handles")
                 mine = ctypes.create_string_buffer(64)
                 _lib.call("mtpb_comm_ipc_handle", comm.handle, mine)
-                handles: list = [None] * ctx.tp_size
-                dist.all_gather_object(handles, bytes(mine.raw), group=ctx.process_group)
-                blob = ctypes.create_string_buffer(b"".join(handles), 64 * ctx.tp_size)
+                all_h = exchange_handles(ctx.process_group, mine.raw, ctx.tp_size)
+                blob = ctypes.create_string_buffer(all_h, 64 * ctx.tp_size)
                 _lib.call("mtpb_comm_open", comm.handle, blob)
                 # every rank mapped every peer before anyone sends
                 dist.barrier(group=ctx.process_group)

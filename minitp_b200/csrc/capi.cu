@@ -23,6 +23,7 @@ namespace {
 thread_local std::string g_err;
 bool g_pdl = true;
 uint32_t g_prefetch_cap = 4u << 20;
+int g_gemv_ctas_per_sm = 2;
 
 int fail(int code, const std::string& msg) {
   g_err = msg;
@@ -116,7 +117,7 @@ int gemv_launch(GemvParams p, cudaStream_t st) {
   }
   if (EPI == kEpiArgmax && p.M > 64) return fail(MTPB_ERR_INVALID, "gemv argmax: M > 64");
   const int sms = sm_count();
-  const int G = std::max(1, std::min(p.units, std::min(sms, kMaxCtas)));
+  const int G = std::max(1, std::min(p.units, std::min(sms * g_gemv_ctas_per_sm, kMaxCtas)));
   const int per = (p.units + G - 1) / G;
   const int groups = (per + RPW - 1) / RPW;
   const int CPR = p.K / VE;
@@ -149,7 +150,9 @@ int gemv_dispatch(int dtype, const GemvParams& p, cudaStream_t st) {
 }
 
 // grid size a GEMV launch will use (producer CTA count of a push site)
-int gemv_grid(int units) { return std::max(1, std::min(units, std::min(sm_count(), kMaxCtas))); }
+int gemv_grid(int units) {
+  return std::max(1, std::min(units, std::min(sm_count() * g_gemv_ctas_per_sm, kMaxCtas)));
+}
 
 GemvParams gemv_base(const void* w, const void* bias, int M, int N, int K, int units) {
   GemvParams p;
@@ -646,6 +649,11 @@ int mtpb_set_pdl(int enable) {
 }
 int mtpb_set_prefetch_cap(uint32_t bytes) {
   g_prefetch_cap = bytes;
+  return MTPB_OK;
+}
+int mtpb_set_gemv_ctas_per_sm(int n) {
+  if (n < 1 || n > 8) return fail(MTPB_ERR_INVALID, "gemv CTAs per SM must be in [1, 8]");
+  g_gemv_ctas_per_sm = n;
   return MTPB_OK;
 }
 

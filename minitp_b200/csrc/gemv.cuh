@@ -331,33 +331,42 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
         for (int r = 0; r < R; ++r) acc[m][r] = 0.f;
 
       if (active) {
-        for (int c = c_beg + lane; c < c_end; c += 64) {
-          const int c2 = c + 32;
-          const bool has2 = c2 < c_end;
-          uint4 wv[2][R];
+        // U chunks x R rows of 16-byte weight loads in flight per lane
+        constexpr int U = (MT <= 2) ? 4 : 2;
+        for (int c0 = c_beg + lane; c0 < c_end; c0 += 32 * U) {
+          uint4 wv[U][R];
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const bool ok = valid[r / UR];
-            wv[0][r] = ok ? ld_stream(W + size_t(rows[r]) * p.K + size_t(c) * VE) : make_uint4(0, 0, 0, 0);
-            wv[1][r] = (ok && has2) ? ld_stream(W + size_t(rows[r]) * p.K + size_t(c2) * VE)
-                                    : make_uint4(0, 0, 0, 0);
+          for (int h = 0; h < U; ++h) {
+            const int c = c0 + 32 * h;
+            const bool okc = c < c_end;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              wv[h][r] = (okc && valid[r / UR]) ? ld_stream(W + size_t(rows[r]) * p.K + size_t(c) * VE)
+                                                : make_uint4(0, 0, 0, 0);
+            }
           }
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int cc = h == 0 ? c : c2;
-            if (h == 1 && !has2) break;
-            float wf[R][VE];
+          for (int h = 0; h < U; ++h) {
+            const int c = c0 + 32 * h;
+            if (c < c_end) {
+              float xf[MT][VE];
 #pragma unroll
-            for (int r = 0; r < R; ++r) unpack(wv[h][r], wf[r]);
+              for (int m = 0; m < MT; ++m) {
+                if (m0 + m < p.M) {
+                  unpack(ld_vec(xs + size_t(m0 + m) * ldxs + size_t(c) * VE), xf[m]);
+                } else {
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              if (m0 + m < p.M) {
-                float xf[VE];
-                unpack(ld_vec(xs + size_t(m0 + m) * ldxs + size_t(cc) * VE), xf);
+                  for (int e = 0; e < VE; ++e) xf[m][e] = 0.f;
+                }
+              }
 #pragma unroll
-                for (int r = 0; r < R; ++r)
+              for (int r = 0; r < R; ++r) {
+                float wf[VE];
+                unpack(wv[h][r], wf);
 #pragma unroll
-                  for (int e = 0; e < VE; ++e) acc[m][r] = fmaf(wf[r][e], xf[e], acc[m][r]);
+                for (int m = 0; m < MT; ++m)
+#pragma unroll
+                  for (int e = 0; e < VE; ++e) acc[m][r] = fmaf(wf[e], xf[m][e], acc[m][r]);
               }
             }
           }

@@ -23,7 +23,8 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, fn, port: int, out_path: str, args: tuple, env: dict) -> None:
+def _worker(rank: int, world: int, fn, port: int, out_path: str, args: tuple, env: dict, init_pg: bool,
+            timeout_s: float) -> None:
     os.environ.update(env)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -35,22 +36,29 @@ def _worker(rank: int, world: int, fn, port: int, out_path: str, args: tuple, en
     torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
     import datetime as dt
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=dt.timedelta(seconds=600))
+    if init_pg:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=dt.timedelta(seconds=timeout_s))
     try:
         result = fn(rank, world, *args)
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
     torch.save(result, f"{out_path}.{rank}")
 
 
-def run_tp(world: int, fn, *args, env: dict | None = None) -> dict[int, object]:
-    """Run ``fn(rank, world, *args)`` on ``world`` Gloo ranks; returns {rank: result}."""
+def run_tp(world: int, fn, *args, env: dict | None = None, init_pg: bool = True,
+           timeout_s: float = 600.0) -> dict[int, object]:
+    """Run ``fn(rank, world, *args)`` on ``world`` Gloo ranks; returns {rank: result}.
+
+    With ``init_pg=False`` the worker creates the process group itself (from
+    the RANK / WORLD_SIZE / MASTER_* environment the harness sets).
+    """
     port = free_port()
     out_path = os.path.join(tempfile.gettempdir(), f"mtpb_tp{world}_{os.getpid()}_{port}")
     try:
         mp.start_processes(
             _worker,
-            args=(world, fn, port, out_path, args, dict(env or {})),
+            args=(world, fn, port, out_path, args, dict(env or {}), init_pg, timeout_s),
             nprocs=world,
             join=True,
             start_method="spawn",
