@@ -207,6 +207,25 @@ int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_cach
                            void* const* v_caches, int cap, int64_t* out_ids, int ld_out,
                            void* logits, void* stream);
 
+/* Decode-step implementation: 0 (default) = the persistent megakernel (one
+ * cooperative launch per token; used when B <= 8 and the shapes fit its
+ * shared-memory plan), 1 = the chain of per-operation kernels. */
+int mtpb_set_decode_impl(int impl);
+
+/* Diagnostic: when `buf` (device uint64[4096]) is not NULL, later megakernel
+ * launches record CTA 0's stage timeline there (%globaltimer ns): [0] start,
+ * [1 + 12 l + e] the 12 stage events of layer l, [1 + 12 L ..] the LM-head and
+ * selection events, [512 + s] the first weight copy of weight stage s,
+ * [1000 ..] the phases of CTA 0's first attention item; the last CTA records
+ * its stage events at [2048 + index]. */
+int mtpb_set_decode_trace(void* buf);
+
+/* Megakernel weight ring: at most `nslot_max` shared-memory slots of `slot_kb`
+ * KiB, at most `inflight` bulk copies outstanding per CTA (0: up to the ring),
+ * `l2_hint` != 0 streams weights with an L2 evict-first policy. Defaults
+ * (8, 32, 2, 1). */
+int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,7 @@
 #include "gemv.cuh"
 #include "minitp_b200.h"
 #include "misc.cuh"
+#include "decode_mk.cuh"
 
 using namespace mtpb;
 
@@ -367,7 +368,16 @@ struct ModelHost {
   void* logits = nullptr;  // [64][V_local] scratch for decode steps without a logits output
   long long* best = nullptr;
   AttnScratch ascr;
+  // decode megakernel state
+  MkLayer* mk_layers = nullptr;  // device copy of the per-layer pointers (+ KV caches)
+  std::vector<MkLayer> mk_host;  // what mk_layers currently holds
+  char* mk_scratch = nullptr;
+  size_t mk_bytes = 0;
 };
+
+int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
+unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
+int g_mk_nslot_max = kMkMaxSlots, g_mk_slot_kb = 32, g_mk_inflight = 2, g_mk_l2hint = 1;
 
 bool capturing(cudaStream_t st) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -628,7 +638,192 @@ int model_forward_t(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
   return MTPB_OK;
 }
 
+// ------------------------------------------------------------------ decode megakernel
+constexpr int kNotEligible = 1;
+
+int smem_optin() {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return v > 0 ? v : 227 * 1024;
+}
+
+// Fill the shape / scratch part of the megakernel parameters; returns
+// kNotEligible when this model or batch does not fit the megakernel.
+int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
+  const mtpb_model_desc& d = mh.d;
+  const size_t tsz = dsize(d.dtype);
+  const int VE = vec_elems(d.dtype);
+  if (M < 1 || M > kMkMaxM) return kNotEligible;
+  if (d.head_dim > 128 || d.head_dim % 2 || d.hq_local % d.hkv_local) return kNotEligible;
+  // attention lanes: head_dim / (16-byte vector) must divide 32 with >= 2 position groups
+  if ((d.head_dim / VE) < 1 || 32 % (d.head_dim / VE) || d.head_dim / VE > 16) return kNotEligible;
+  if (d.hidden % VE || d.inter_local % VE || (d.hq_local * d.head_dim) % VE) return kNotEligible;
+  const size_t slot = size_t(g_mk_slot_kb) * 1024;
+  if (2 * size_t(d.hidden) * tsz > slot || size_t(d.inter_local) * tsz > slot ||
+      size_t(d.hq_local) * d.head_dim * tsz > slot)
+    return kNotEligible;
+  const int G = sm_count();
+  if (G > kMaxCtas) return kNotEligible;
+  std::memset(&p, 0, sizeof(p));
+  p.L = d.n_layers;
+  p.H = d.hidden;
+  p.I = d.inter_local;
+  p.hq = d.hq_local;
+  p.hkv = d.hkv_local;
+  p.hd = d.head_dim;
+  p.M = M;
+  p.kv_cap = cap;
+  p.xin_cols = std::max(d.hq_local * d.head_dim, d.inter_local);
+  int ns = (cap + 31) / 32;
+  ns = std::min(ns, 64);
+  // attention items must fit the flag array, and the split-merge weights the
+  // per-warp attention scratch they reuse (kMkCons * 3 * head_dim floats)
+  const size_t merge_cap = size_t(kMkCons) * 3 * d.head_dim;
+  while (ns > 1 && (size_t(M) * d.hq_local * ns > size_t(kLfSlots) || size_t(M) * d.hq_local * ns > merge_cap))
+    ns /= 2;
+  if (size_t(M) * d.hq_local * ns > size_t(kLfSlots) || size_t(M) * d.hq_local * ns > merge_cap) return kNotEligible;
+  p.nsplit = std::max(ns, 1);
+  p.slot_bytes = int(slot);
+  // as many ring slots as shared memory allows (at least 2)
+  const int budget = smem_optin() - 2048;  // static shared memory of the kernel
+  p.nslot = 0;
+  MkLayout lay = mk_layout(p, tsz);
+  const size_t fixed = lay.ring;
+  int nslot = int((size_t(budget) - std::min(size_t(budget), fixed)) / slot);
+  nslot = std::min(nslot, std::min(kMkMaxSlots, g_mk_nslot_max));
+  if (nslot < 2) return kNotEligible;
+  p.nslot = nslot;
+  p.inflight = std::min(g_mk_inflight, nslot - 1);
+  p.l2_hint = g_mk_l2hint;
+  lay = mk_layout(p, tsz);
+  *smem_out = lay.total;
+  // scratch: qkv_buf, att_part, act_buf, lm_best, lflags
+  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * d.head_dim;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t b_qkv = up(size_t(kMkMaxM) * nq * tsz);
+  const size_t b_att = up(size_t(kMkMaxM) * d.hq_local * 64 * (d.head_dim + 2) * sizeof(float));
+  const size_t b_act = up(size_t(kMkMaxM) * d.inter_local * tsz);
+  const size_t b_best = up(size_t(kMaxCtas) * kMkMaxM * sizeof(long long));
+  const size_t b_flags = up(size_t(kLfKinds) * kLfSlots * sizeof(uint32_t));
+  const size_t total = b_qkv + b_att + b_act + b_best + b_flags;
+  if (mh.mk_bytes < total) return kNotEligible;  // reserved by mk_reserve
+  char* s = mh.mk_scratch;
+  p.qkv_buf = s;
+  s += b_qkv;
+  p.att_part = reinterpret_cast<float*>(s);
+  s += b_att;
+  p.act_buf = s;
+  s += b_act;
+  p.lm_best = reinterpret_cast<long long*>(s);
+  s += b_best;
+  p.lflags = reinterpret_cast<uint32_t*>(s);
+  return MTPB_OK;
+}
+
+int mk_reserve(ModelHost& mh) {
+  if (mh.mk_scratch) return MTPB_OK;
+  const mtpb_model_desc& d = mh.d;
+  const size_t tsz = dsize(d.dtype);
+  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * d.head_dim;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t total = up(size_t(kMkMaxM) * nq * tsz) +
+                       up(size_t(kMkMaxM) * d.hq_local * 64 * (d.head_dim + 2) * sizeof(float)) +
+                       up(size_t(kMkMaxM) * d.inter_local * tsz) + up(size_t(kMaxCtas) * kMkMaxM * 8) +
+                       up(size_t(kLfKinds) * kLfSlots * 4);
+  MTPB_CUDA(cudaMalloc(&mh.mk_scratch, total));
+  MTPB_CUDA(cudaMemset(mh.mk_scratch, 0, total));
+  MTPB_CUDA(cudaMalloc(&mh.mk_layers, sizeof(MkLayer) * d.n_layers));
+  mh.mk_bytes = total;
+  return MTPB_OK;
+}
+
+template <typename T, int MT>
+int mk_launch_t(const MkParams& p, size_t smem, cudaStream_t st) {
+  auto kern = decode_mk_kernel<T, MT>;
+  static size_t smem_set = 0;  // the attribute is raised outside graph capture only
+  if (smem > smem_set) {
+    if (capturing(st)) return fail(MTPB_ERR_INVALID, "decode step: run one step eagerly before graph capture");
+    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    smem_set = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kMkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MTPB_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+  return MTPB_OK;
+}
+
+// One decode step through the megakernel; kNotEligible when it cannot run it.
+int mk_decode(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
+  if (g_decode_impl != 0 || !a.decode || a.T != 1) return kNotEligible;
+  const mtpb_model_desc& d = mh.d;
+  if (!capturing(st)) MTPB_TRY(mk_reserve(mh));
+  if (!mh.mk_scratch) return kNotEligible;
+  MkParams p;
+  size_t smem = 0;
+  if (mk_plan(mh, a.B, a.cap, p, &smem) != MTPB_OK) return kNotEligible;
+  // per-layer pointers (weights + this call's KV caches), uploaded when they change
+  std::vector<MkLayer> want(d.n_layers);
+  for (int l = 0; l < d.n_layers; ++l) {
+    const mtpb_layer_desc& ly = mh.layers[l];
+    want[l] = MkLayer{ly.ln1, ly.qkv_w, ly.qkv_b, ly.o_w, ly.ln2, ly.gu_w, ly.down_w, a.kc[l], a.vc[l]};
+  }
+  if (want.size() != mh.mk_host.size() ||
+      std::memcmp(want.data(), mh.mk_host.data(), sizeof(MkLayer) * want.size()) != 0) {
+    if (capturing(st)) return fail(MTPB_ERR_INVALID, "decode step: KV caches changed during graph capture");
+    MTPB_CUDA(cudaMemcpy(mh.mk_layers, want.data(), sizeof(MkLayer) * want.size(), cudaMemcpyHostToDevice));
+    mh.mk_host = want;
+  }
+  p.comm = mh.comm->dev;
+  p.layers = mh.mk_layers;
+  p.vstart = d.vocab_start;
+  p.vend = d.vocab_end;
+  p.vocab = d.vocab_size;
+  p.embed = d.embed;
+  p.lm_head = d.lm_head;
+  p.final_norm = d.final_norm;
+  p.cos_tab = d.cos_tab;
+  p.sin_tab = d.sin_tab;
+  p.rope_len = d.rope_len;
+  p.eps = d.eps;
+  p.scale = 1.0f / std::sqrt(float(d.head_dim));
+  p.pos_ptr = a.pos_ptr;
+  p.tok = a.tok_out;
+  p.out_ids = a.out_ids;
+  p.ld_out = a.ld_out;
+  p.logits = a.logits;
+  p.budget_ns = mh.comm->dev.timeout_ns;
+  p.trace = g_mk_trace;
+  const int MT = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
+  if (d.dtype == MTPB_BF16) {
+    switch (MT) {
+      case 1: return mk_launch_t<bf16, 1>(p, smem, st);
+      case 2: return mk_launch_t<bf16, 2>(p, smem, st);
+      case 4: return mk_launch_t<bf16, 4>(p, smem, st);
+      default: return mk_launch_t<bf16, 8>(p, smem, st);
+    }
+  }
+  switch (MT) {
+    case 1: return mk_launch_t<float, 1>(p, smem, st);
+    case 2: return mk_launch_t<float, 2>(p, smem, st);
+    case 4: return mk_launch_t<float, 4>(p, smem, st);
+    default: return mk_launch_t<float, 8>(p, smem, st);
+  }
+}
+
 int model_forward(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
+  if (a.decode) {
+    const int r = mk_decode(mh, a, st);
+    if (r != kNotEligible) return r;
+  }
   if (mh.d.dtype == MTPB_BF16) return model_forward_t<bf16>(mh, a, st);
   if (mh.d.dtype == MTPB_F32) return model_forward_t<float>(mh, a, st);
   return fail(MTPB_ERR_INVALID, "unsupported dtype");
@@ -997,7 +1192,30 @@ int mtpb_model_destroy(void* model) {
   cudaFree(mh->ascr.part_o);
   cudaFree(mh->ascr.part_ml);
   cudaFree(mh->ascr.counters);
+  cudaFree(mh->mk_scratch);
+  cudaFree(mh->mk_layers);
   delete mh;
+  return MTPB_OK;
+}
+
+int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint) {
+  if (nslot_max < 2 || nslot_max > kMkMaxSlots || slot_kb < 4 || slot_kb > 128 || slot_kb % 4 || inflight < 0)
+    return fail(MTPB_ERR_INVALID, "decode ring: 2 <= nslot <= 8, 4 <= slot_kb <= 128 (multiple of 4), inflight >= 0");
+  g_mk_nslot_max = nslot_max;
+  g_mk_slot_kb = slot_kb;
+  g_mk_inflight = inflight;
+  g_mk_l2hint = l2_hint ? 1 : 0;
+  return MTPB_OK;
+}
+
+int mtpb_set_decode_trace(void* buf) {
+  g_mk_trace = static_cast<unsigned long long*>(buf);
+  return MTPB_OK;
+}
+
+int mtpb_set_decode_impl(int impl) {
+  if (impl != 0 && impl != 1) return fail(MTPB_ERR_INVALID, "decode impl must be 0 (megakernel) or 1 (kernel chain)");
+  g_decode_impl = impl;
   return MTPB_OK;
 }
 

@@ -90,32 +90,19 @@ __device__ __forceinline__ void signal_peers(const Comm& c, int chan, uint32_t s
 
 // Consumer side: wait until producer CTAs [0, nprod) of every rank signalled
 // `seq`. With world == 1 nothing needs waiting (stream order suffices).
+// (warp 0 polls; every thread of the block must call it)
 __device__ __forceinline__ bool wait_peers(const Comm& c, int chan, uint32_t seq, int nprod) {
   if (c.world == 1) return true;
   __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
-  const int par = seq & 1;
-  bool ok = true;
-  const int n = c.world * nprod;
-  uint64_t t0 = 0;
-  for (int i = threadIdx.x; i < n && ok; i += blockDim.x) {
-    const int src = i / nprod, cta = i - src * nprod;
-    const uint32_t* f = c.flag(c.rank, chan, par, src, cta);
-    uint32_t spins = 0;
-    while (!seq_reached(ld_acquire_sys(f), seq)) {
-      if ((++spins & 63u) == 0) {
-        if (t0 == 0) t0 = global_ns();
-        if (ld_volatile_u32(c.status()) != 0 || global_ns() - t0 > c.timeout_ns) {
-          ok = false;
-          break;
-        }
-      }
+  if (threadIdx.x < 32) {
+    const int par = seq & 1;
+    bool ok = true;
+    for (int src = 0; src < c.world && ok; ++src)
+      ok = warp_poll_flags(c.flag(c.rank, chan, par, src, 0), nprod, seq, true, c.status(), c.timeout_ns);
+    if (threadIdx.x == 0) {
+      s_ok = ok ? 1 : 0;
+      if (!ok) atomicOr(c.status(), kStatusTimeout);
     }
-  }
-  if (!ok) {
-    atomicOr(c.status(), kStatusTimeout);
-    s_ok = 0;
   }
   __syncthreads();
   const bool res = s_ok != 0;
@@ -128,22 +115,14 @@ __device__ __forceinline__ bool wait_peers(const Comm& c, int chan, uint32_t seq
 __device__ __forceinline__ bool wait_peers_cta(const Comm& c, int chan, uint32_t seq, int cta) {
   if (c.world == 1) return true;
   __shared__ int s_ok2;
-  if (threadIdx.x == 0) s_ok2 = 1;
-  __syncthreads();
-  const int par = seq & 1;
-  if (threadIdx.x < c.world) {
-    const uint32_t* f = c.flag(c.rank, chan, par, threadIdx.x, cta);
-    uint32_t spins = 0;
-    uint64_t t0 = 0;
-    while (!seq_reached(ld_acquire_sys(f), seq)) {
-      if ((++spins & 63u) == 0) {
-        if (t0 == 0) t0 = global_ns();
-        if (ld_volatile_u32(c.status()) != 0 || global_ns() - t0 > c.timeout_ns) {
-          atomicOr(c.status(), kStatusTimeout);
-          s_ok2 = 0;
-          break;
-        }
-      }
+  if (threadIdx.x < 32) {
+    const int par = seq & 1;
+    bool ok = true;
+    for (int src = 0; src < c.world && ok; ++src)
+      ok = warp_poll_flags(c.flag(c.rank, chan, par, src, cta), 1, seq, true, c.status(), c.timeout_ns);
+    if (threadIdx.x == 0) {
+      s_ok2 = ok ? 1 : 0;
+      if (!ok) atomicOr(c.status(), kStatusTimeout);
     }
   }
   __syncthreads();

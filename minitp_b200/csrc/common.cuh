@@ -126,36 +126,82 @@ __device__ __forceinline__ bool seq_reached(uint32_t v, uint32_t seq) {
   return static_cast<int32_t>(v - seq) >= 0;
 }
 
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// One warp polls flags[0, n) until every flag reached `seq` (wrap-safe),
+// with 16-byte loads when `flags` is 16-byte aligned and a short sleep
+// between rounds so that many CTAs polling at once do not flood L2. After
+// success an acquire fence at `sys` (else gpu) scope orders the caller's
+// later reads after the producers' releases. Bounded: returns false when
+// `timeout_ns` passed, *status became non-zero or *abort became non-zero.
+// All lanes of the warp must call it; all return the same value.
+__device__ __forceinline__ bool warp_poll_flags(const uint32_t* flags, int n, uint32_t seq, bool sys,
+                                                uint32_t* status, uint64_t timeout_ns,
+                                                const volatile int* abort = nullptr) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = (reinterpret_cast<uintptr_t>(flags) & 15u) == 0;
+  uint64_t t0 = 0;
+  uint32_t round = 0;
+  while (true) {
+    bool mine = true;
+    if (vec) {
+      for (int i = lane * 4; i < n; i += 128) {
+        if (i + 3 < n) {
+          const uint4 v = ld_volatile_v4(flags + i);
+          mine = mine && seq_reached(v.x, seq) && seq_reached(v.y, seq) && seq_reached(v.z, seq) &&
+                 seq_reached(v.w, seq);
+        } else {
+          for (int j = i; j < n; ++j) mine = mine && seq_reached(ld_volatile_u32(flags + j), seq);
+        }
+      }
+    } else {
+      for (int i = lane; i < n; i += 32) mine = mine && seq_reached(ld_volatile_u32(flags + i), seq);
+    }
+    if (__all_sync(0xffffffffu, mine)) break;
+    ++round;
+    if ((round & 7u) == 0) {
+      bool bad = false;
+      if (lane == 0) {
+        if (t0 == 0) t0 = global_ns();
+        bad = ld_volatile_u32(status) != 0 || global_ns() - t0 > timeout_ns || (abort && *abort);
+      }
+      if (__shfl_sync(0xffffffffu, bad ? 1 : 0, 0)) return false;
+    }
+    if (round > 4) __nanosleep(round > 64 ? 256 : 64);
+  }
+  if (sys) {
+    fence_sys();
+  } else {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
+  return true;
+}
+
 // Block-wide bounded wait until flags[i] >= seq for every i in [0, n).
 // Every thread of the block must call it. Returns false (after recording
 // kStatusTimeout in *status) when the budget runs out or when another wait
 // already failed; the caller then skips its work and returns.
-__device__ __forceinline__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t seq,
+// Every thread of the block calls it; warp 0 polls, the others wait at the
+// barrier. Records kStatusTimeout on failure.
+__device__ __forceinline__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t seq, bool sys,
                                                  uint32_t* status, uint64_t timeout_ns) {
   __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
-  bool ok = true;
-  uint64_t t0 = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    uint32_t spins = 0;
-    while (!seq_reached(ld_acquire_sys(flags + i), seq)) {
-      if ((++spins & 63u) == 0) {
-        if (t0 == 0) t0 = global_ns();
-        if (ld_volatile_u32(status) != 0 || global_ns() - t0 > timeout_ns) {
-          ok = false;
-          break;
-        }
-      }
+  if (threadIdx.x < 32) {
+    const bool ok = warp_poll_flags(flags, n, seq, sys, status, timeout_ns);
+    if (threadIdx.x == 0) {
+      s_ok = ok ? 1 : 0;
+      if (!ok) atomicOr(status, kStatusTimeout);
     }
-    if (!ok) break;
-  }
-  if (!ok) {
-    atomicOr(status, kStatusTimeout);
-    s_ok = 0;
   }
   __syncthreads();
-  bool res = s_ok != 0;
+  const bool res = s_ok != 0;
   __syncthreads();
   return res;
 }
