@@ -2,8 +2,9 @@
 
 ``GenerationState`` keeps the reference API (prefill / select_next / append /
 decode_step, ``out_ids``, ``positions_buf``, ``cursor``). ``generate_greedy``
-with a fixed length (``early_stop=False``, or no EOS id) runs the decode loop
-as replays of one CUDA graph. The graph holds one captured
+(distributed argmax, up to 64 rows) runs the decode loop as replays of one
+CUDA graph; with an EOS id and ``early_stop`` it checks on the host after
+each replay whether every row finished, as the reference loop does. The graph holds one captured
 ``mtpb_model_decode_step``: the embedding of the current token, all layers,
 the LM head with the packed-key argmax, the NVLink exchange of the winners,
 and the write of the token to ``out_ids[:, pos + 1]`` with the position
@@ -149,6 +150,42 @@ class GenerationState:
                     self.device_step()
         return self.out_ids
 
+    def run_until_eos(self, eos_token_id: int, use_graph: bool = True) -> torch.Tensor:
+        """Greedy generation that stops once every row emitted EOS.
+
+        The reference loop (generation.py:147-171): a finished row keeps
+        emitting EOS and the loop ends at the first step where all rows are
+        finished (one host check per step, as there). The steps themselves are
+        the same device decode steps as ``run_fixed``, so both loops produce
+        the same ids up to the stop.
+        """
+        dev = self.out_ids.device
+        self.eos = eos_token_id
+        self.finished = torch.zeros(self.batch, dtype=torch.bool, device=dev)
+        eos_t = torch.tensor(eos_token_id, dtype=torch.long, device=dev)
+        tok = self.select_next(self.prefill(last_only=True))
+        for step in range(self.max_new_tokens):
+            if step > 0:
+                if self._graph is not None:
+                    self.graph_step()
+                else:
+                    self.device_step()
+                    if use_graph and step + 1 < self.max_new_tokens:
+                        self.capture()
+                tok = self._tok
+            tok = torch.where(self.finished, eos_t, tok)
+            self.finished |= tok == eos_token_id
+            if step == 0:
+                self.append(tok)
+            else:
+                self.out_ids[:, self.cursor - 1] = tok
+                self._tok.copy_(tok)
+            if bool(self.finished.all()):
+                break
+            if step == 0 and self.max_new_tokens > 1:
+                self.start_device_decode(tok)
+        return self.out_ids[:, : self.cursor]
+
     def release(self) -> None:
         self._graph = None
 
@@ -174,10 +211,14 @@ def generate_greedy(
                             kv_init=kv_init)
     b = input_ids.shape[0]
     fixed = not (early_stop and eos_token_id is not None)
-    if fixed and distributed_argmax and b <= 64:
-        out = state.run_fixed(use_graph=True)
+    if distributed_argmax and b <= 64:
+        if fixed:
+            out = state.run_fixed(use_graph=True)
+            out = out if not early_stop else out[:, : state.cursor]
+        else:
+            out = state.run_until_eos(eos_token_id, use_graph=True)
         state.release()
-        return out if not early_stop else out[:, : state.cursor]
+        return out
     if early_stop and eos_token_id is not None:
         state.eos = eos_token_id
         state.finished = torch.zeros(b, dtype=torch.bool, device=input_ids.device)
