@@ -109,6 +109,29 @@ int mtpb_attention(const void* q, const void* k_cache, const void* v_cache, void
                    int hq, int hkv, int hd, int cap, int cache_len, int dtype, void* comm,
                    void* stream);
 
+/* Same computation and arguments as mtpb_attention (without the
+ * communicator), for callers that must not allocate device memory: hosts
+ * whose caching allocator or memory budget owns every device byte, and
+ * latency-bound loops that cannot afford the device-wide synchronisation
+ * of cudaMalloc/cudaFree. It has no counterpart in the reference.
+ *
+ * mtpb_attention allocates its split-KV scratch on first use; this variant
+ * keeps it in a fixed device array of MTPB_NOALLOC_SCRATCH_BYTES (4 MiB)
+ * compiled into the library, which every GPU that loads the library holds
+ * until the process exits. It calls no cudaMalloc or cudaFree. A shape whose
+ * scratch would exceed the array fails with MTPB_ERR_INVALID and a message
+ * giving the bytes it needs (decode shapes need well under 1 MiB; shapes
+ * with B*T*hkv >= the SM count need none). The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. All calls
+ * on a device share the one array: calls that overlap on the GPU (on
+ * different streams, or from several threads) race and must be ordered by
+ * the caller. Each call clears the counters it needs at its start. */
+#define MTPB_NOALLOC_SCRATCH_BYTES (4u << 20)
+int mtpb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
+                           int T, int hq, int hkv, int hd, int cap, int cache_len, int dtype,
+                           void* stream);
+
 /* RMSNorm: y = T(x * rsqrt(mean(x^2) + eps) * w) in fp32 math.
  * ref: minitp/layer.py:36-42. */
 int mtpb_rmsnorm(const void* x, const void* w, void* y, int rows, int H, float eps, int dtype,

@@ -84,6 +84,8 @@ SIGNATURES: dict[str, tuple] = {
                               c_int, c_void_p, c_void_p]),
     "mtpb_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_void_p, c_void_p]),
+    "mtpb_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                       c_int, c_int, c_int, c_void_p]),
     "mtpb_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_void_p]),
     "mtpb_allreduce": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "mtpb_allreduce_residual_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -1264,3 +1264,73 @@ int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_cach
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ attention, no allocation
+// mtpb_attention_noalloc keeps its split-KV partials in this file-scope device
+// array instead of memory the library allocates. The array is part of the
+// module image: every GPU that loads the library holds it until the process
+// exits. Layout of one call (offsets rounded up to 256 bytes):
+//   [0, 256)              status word of the kernel (never read back)
+//   counters u32[M*hkv]   last-CTA merge counters, cleared by every call
+//   part_ml  f32[M*hq*splits*2], part_o f32[M*hq*splits*hd]
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[MTPB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// Device address of g_attn_noalloc_scratch on the current device, looked up
+// once per device (host code cannot use the symbol itself as a pointer).
+int noalloc_scratch_addr(char** out) {
+  static std::mutex mu;
+  static char* per_dev[64] = {};
+  int dev = 0;
+  MTPB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MTPB_ERR_INVALID, "attention_noalloc: device ordinal above 63");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!per_dev[dev]) {
+    void* p = nullptr;
+    MTPB_CUDA(cudaGetSymbolAddress(&p, g_attn_noalloc_scratch));
+    per_dev[dev] = static_cast<char*>(p);
+  }
+  *out = per_dev[dev];
+  return MTPB_OK;
+}
+
+}  // namespace
+
+extern "C" int mtpb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
+                                      int T, int hq, int hkv, int hd, int cap, int cache_len, int dtype,
+                                      void* stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(MTPB_ERR_INVALID, "attention_noalloc: null tensor");
+  if (B <= 0 || T <= 0 || hq <= 0 || hkv <= 0 || hd <= 0 || cap <= 0 || cache_len < 0)
+    return fail(MTPB_ERR_INVALID, "attention_noalloc: sizes must be positive");
+  if (hq % hkv != 0) return fail(MTPB_ERR_INVALID, "attention: hq must be a multiple of hkv");
+  if (cache_len + T > cap) return fail(MTPB_ERR_INVALID, "attention: cache_len + T exceeds the cache capacity");
+  const int M = B * T, G = hq / hkv;
+  int chunk = 0;
+  const int ns = attn_choose_splits(M, hkv, G, cap, hd, &chunk);
+  const size_t n_ctr = size_t(M) * hkv, n_ml = size_t(M) * hq * ns * 2, n_o = size_t(M) * hq * ns * hd;
+  const size_t off_ctr = 256, off_ml = off_ctr + round256(n_ctr * 4), off_o = off_ml + round256(n_ml * 4);
+  const size_t need = off_o + n_o * 4;
+  if (ns > 1 && need > MTPB_NOALLOC_SCRATCH_BYTES)
+    return fail(MTPB_ERR_INVALID, "attention_noalloc: this shape needs " + std::to_string(need) +
+                                      " bytes of scratch; the static scratch holds " +
+                                      std::to_string(size_t(MTPB_NOALLOC_SCRATCH_BYTES)) +
+                                      " (use fewer rows or a smaller cache capacity, or mtpb_attention)");
+  char* base = nullptr;
+  MTPB_TRY(noalloc_scratch_addr(&base));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // A view sized exactly to this call's needs: attn_run finds it big enough
+  // and never allocates.
+  AttnScratch view;
+  view.counters = reinterpret_cast<uint32_t*>(base + off_ctr);
+  view.part_ml = reinterpret_cast<float*>(base + off_ml);
+  view.part_o = reinterpret_cast<float*>(base + off_o);
+  view.ctr_elems = n_ctr;
+  view.ml_elems = n_ml;
+  view.o_elems = n_o;
+  if (ns > 1) MTPB_CUDA(cudaMemsetAsync(view.counters, 0, n_ctr * 4, st));
+  return attn_run(dtype, q, k_cache, v_cache, out, B, T, hq, hkv, hd, cap, nullptr, cache_len, view,
+                  reinterpret_cast<uint32_t*>(base), st);
+}
