@@ -249,6 +249,10 @@ int mtpb_set_decode_trace(void* buf);
  * (8, 32, 2, 1). */
 int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint);
 
+/* Megakernel: nanoseconds a thread sleeps between two polls of a data word
+ * that has not arrived yet (0, the default: poll back to back). */
+int mtpb_set_decode_spin(int backoff_ns);
+
 #ifdef __cplusplus
 }
 #endif

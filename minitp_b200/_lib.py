@@ -105,6 +105,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_set_decode_impl": (c_int, [c_int]),
     "mtpb_set_decode_trace": (c_int, [c_void_p]),
     "mtpb_set_decode_ring": (c_int, [c_int, c_int, c_int, c_int]),
+    "mtpb_set_decode_spin": (c_int, [c_int]),
 }
 
 _lib: ctypes.CDLL | None = None

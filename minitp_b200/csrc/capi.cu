@@ -378,6 +378,7 @@ struct ModelHost {
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
 int g_mk_nslot_max = kMkMaxSlots, g_mk_slot_kb = 32, g_mk_inflight = 2, g_mk_l2hint = 1;
+uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -648,90 +649,98 @@ int smem_optin() {
   return v > 0 ? v : 227 * 1024;
 }
 
+// Device scratch of the megakernel (LL words), sized for the largest batch.
+struct MkScratch {
+  size_t qkv, att, act, lm, total;
+};
+
+MkScratch mk_scratch_layout(const mtpb_model_desc& d) {
+  const int P = d.dtype == MTPB_BF16 ? 2 : 1;
+  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * d.head_dim;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  MkScratch s;
+  s.qkv = up(size_t(kMkMaxM) * (nq / P) * 8);
+  s.att = up(size_t(kMkMaxM) * d.hq_local * kMkMaxSplits * (d.head_dim + 2) * 8);
+  s.act = up(size_t(kMkMaxM) * (d.inter_local / P) * 8);
+  s.lm = up(size_t(kMaxCtas) * kMkMaxM * 16);
+  s.total = s.qkv + s.att + s.act + s.lm;
+  return s;
+}
+
 // Fill the shape / scratch part of the megakernel parameters; returns
 // kNotEligible when this model or batch does not fit the megakernel.
 int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   const mtpb_model_desc& d = mh.d;
   const size_t tsz = dsize(d.dtype);
   const int VE = vec_elems(d.dtype);
+  const int P = d.dtype == MTPB_BF16 ? 2 : 1;
+  const int hd = d.head_dim;
   if (M < 1 || M > kMkMaxM) return kNotEligible;
-  if (d.head_dim > 128 || d.head_dim % 2 || d.hq_local % d.hkv_local) return kNotEligible;
-  // attention lanes: head_dim / (16-byte vector) must divide 32 with >= 2 position groups
-  if ((d.head_dim / VE) < 1 || 32 % (d.head_dim / VE) || d.head_dim / VE > 16) return kNotEligible;
-  if (d.hidden % VE || d.inter_local % VE || (d.hq_local * d.head_dim) % VE) return kNotEligible;
+  // head_dim: a power of two in [16, 128] (lane-rotated 16-byte chunks)
+  if (hd < 16 || hd > 128 || (hd & (hd - 1)) || d.hq_local % d.hkv_local) return kNotEligible;
+  // 16-byte weight rows, and rows of whole LL pairs
+  if (d.hidden % VE || d.inter_local % VE || (d.hq_local * hd) % VE) return kNotEligible;
+  if (d.hidden % (2 * P) || d.inter_local % (2 * P)) return kNotEligible;
   const size_t slot = size_t(g_mk_slot_kb) * 1024;
-  if (2 * size_t(d.hidden) * tsz > slot || size_t(d.inter_local) * tsz > slot ||
-      size_t(d.hq_local) * d.head_dim * tsz > slot)
+  // one GEMV unit per ring slot at least: gate/up (2P rows of H), down (P rows of I), o_proj
+  if (size_t(2 * P) * d.hidden * tsz > slot || size_t(P) * d.inter_local * tsz > slot ||
+      size_t(P) * d.hq_local * hd * tsz > slot)
     return kNotEligible;
   const int G = sm_count();
   if (G > kMaxCtas) return kNotEligible;
+  const int ns = (cap + kMkSplit - 1) / kMkSplit;
+  if (ns < 1 || ns > kMkMaxSplits) return kNotEligible;
+  // AllReduce-site words of one batch must fit a communicator slot
+  if (size_t(M) * (d.hidden / P) * 8 > mh.comm->dev.slot_bytes) return kNotEligible;
   std::memset(&p, 0, sizeof(p));
   p.L = d.n_layers;
   p.H = d.hidden;
   p.I = d.inter_local;
   p.hq = d.hq_local;
   p.hkv = d.hkv_local;
-  p.hd = d.head_dim;
+  p.hd = hd;
   p.M = M;
   p.kv_cap = cap;
-  p.xin_cols = std::max(d.hq_local * d.head_dim, d.inter_local);
-  int ns = (cap + 31) / 32;
-  ns = std::min(ns, 64);
-  // attention items must fit the flag array, and the split-merge weights the
-  // per-warp attention scratch they reuse (kMkCons * 3 * head_dim floats)
-  const size_t merge_cap = size_t(kMkCons) * 3 * d.head_dim;
-  while (ns > 1 && (size_t(M) * d.hq_local * ns > size_t(kLfSlots) || size_t(M) * d.hq_local * ns > merge_cap))
-    ns /= 2;
-  if (size_t(M) * d.hq_local * ns > size_t(kLfSlots) || size_t(M) * d.hq_local * ns > merge_cap) return kNotEligible;
-  p.nsplit = std::max(ns, 1);
+  p.nsplit = ns;
+  p.xin_cols = std::max(d.hq_local * hd, d.inter_local);
+  p.wsc_floats = kMkCons * 3 * hd + 2 * M * d.hq_local * ns;
   p.slot_bytes = int(slot);
-  // as many ring slots as shared memory allows (at least 2)
-  const int budget = smem_optin() - 2048;  // static shared memory of the kernel
-  p.nslot = 0;
-  MkLayout lay = mk_layout(p, tsz);
-  const size_t fixed = lay.ring;
-  int nslot = int((size_t(budget) - std::min(size_t(budget), fixed)) / slot);
-  nslot = std::min(nslot, std::min(kMkMaxSlots, g_mk_nslot_max));
+  // stage every attention item of a CTA when shared memory allows; the ring
+  // takes the rest (at least 2 slots)
+  const int per_cta = (M * d.hq_local * ns + G - 1) / G;
+  const int budget = smem_optin() - 4096;  // static shared memory of the kernel
+  int stage = std::min(kMkMaxStage, per_cta);
+  int nslot = 0;
+  for (;;) {
+    p.att_stage = stage;
+    p.nslot = 0;
+    const size_t fixed = mk_layout(p, tsz).ring;
+    nslot = fixed < size_t(budget) ? int((size_t(budget) - fixed) / slot) : 0;
+    nslot = std::min(nslot, std::min(kMkMaxSlots, g_mk_nslot_max));
+    if (nslot >= 2 || stage == 0) break;
+    stage /= 2;
+  }
   if (nslot < 2) return kNotEligible;
   p.nslot = nslot;
   p.inflight = std::min(g_mk_inflight, nslot - 1);
   p.l2_hint = g_mk_l2hint;
-  lay = mk_layout(p, tsz);
-  *smem_out = lay.total;
-  // scratch: qkv_buf, att_part, act_buf, lm_best, lflags
-  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * d.head_dim;
-  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-  const size_t b_qkv = up(size_t(kMkMaxM) * nq * tsz);
-  const size_t b_att = up(size_t(kMkMaxM) * d.hq_local * 64 * (d.head_dim + 2) * sizeof(float));
-  const size_t b_act = up(size_t(kMkMaxM) * d.inter_local * tsz);
-  const size_t b_best = up(size_t(kMaxCtas) * kMkMaxM * sizeof(long long));
-  const size_t b_flags = up(size_t(kLfKinds) * kLfSlots * sizeof(uint32_t));
-  const size_t total = b_qkv + b_att + b_act + b_best + b_flags;
-  if (mh.mk_bytes < total) return kNotEligible;  // reserved by mk_reserve
+  *smem_out = mk_layout(p, tsz).total;
+  const MkScratch sl = mk_scratch_layout(d);
+  if (mh.mk_bytes < sl.total) return kNotEligible;  // reserved by mk_reserve
   char* s = mh.mk_scratch;
-  p.qkv_buf = s;
-  s += b_qkv;
-  p.att_part = reinterpret_cast<float*>(s);
-  s += b_att;
-  p.act_buf = s;
-  s += b_act;
-  p.lm_best = reinterpret_cast<long long*>(s);
-  s += b_best;
-  p.lflags = reinterpret_cast<uint32_t*>(s);
+  p.qkv_ll = reinterpret_cast<uint64_t*>(s);
+  p.att_ll = reinterpret_cast<uint64_t*>(s + sl.qkv);
+  p.act_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att);
+  p.lm_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att + sl.act);
   return MTPB_OK;
 }
 
 int mk_reserve(ModelHost& mh) {
   if (mh.mk_scratch) return MTPB_OK;
   const mtpb_model_desc& d = mh.d;
-  const size_t tsz = dsize(d.dtype);
-  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * d.head_dim;
-  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-  const size_t total = up(size_t(kMkMaxM) * nq * tsz) +
-                       up(size_t(kMkMaxM) * d.hq_local * 64 * (d.head_dim + 2) * sizeof(float)) +
-                       up(size_t(kMkMaxM) * d.inter_local * tsz) + up(size_t(kMaxCtas) * kMkMaxM * 8) +
-                       up(size_t(kLfKinds) * kLfSlots * 4);
+  const size_t total = mk_scratch_layout(d).total;
   MTPB_CUDA(cudaMalloc(&mh.mk_scratch, total));
+  // zero words carry sequence number 0, which no step uses
   MTPB_CUDA(cudaMemset(mh.mk_scratch, 0, total));
   MTPB_CUDA(cudaMalloc(&mh.mk_layers, sizeof(MkLayer) * d.n_layers));
   mh.mk_bytes = total;
@@ -801,6 +810,7 @@ int mk_decode(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
   p.ld_out = a.ld_out;
   p.logits = a.logits;
   p.budget_ns = mh.comm->dev.timeout_ns;
+  p.spin_ns = g_mk_spin_ns;
   p.trace = g_mk_trace;
   const int MT = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
   if (d.dtype == MTPB_BF16) {
@@ -1205,6 +1215,12 @@ int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint) 
   g_mk_slot_kb = slot_kb;
   g_mk_inflight = inflight;
   g_mk_l2hint = l2_hint ? 1 : 0;
+  return MTPB_OK;
+}
+
+int mtpb_set_decode_spin(int backoff_ns) {
+  if (backoff_ns < 0 || backoff_ns > 100000) return fail(MTPB_ERR_INVALID, "decode spin back-off: 0 .. 100000 ns");
+  g_mk_spin_ns = uint32_t(backoff_ns);
   return MTPB_OK;
 }
 

@@ -18,14 +18,16 @@
 // Channel 0 carries the model's collectives; their sequence numbers come from
 // a device step counter so a captured CUDA graph can replay them. Channel 1
 // carries standalone collectives (all_reduce, the fused AR+RMSNorm op), whose
-// sequence numbers come from a device call counter.
+// sequence numbers come from a device call counter. Channel 2 belongs to the
+// decode megakernel, whose data words carry their own sequence numbers
+// (LL words) and need no flags.
 #pragma once
 
 #include "common.cuh"
 
 namespace mtpb {
 
-constexpr int kChannels = 2;
+constexpr int kChannels = 3;
 constexpr int kMaxCtas = 1024;
 constexpr size_t kCtlBytes = 4096;
 constexpr size_t kFlagBytes = size_t(kChannels) * 2 * kMaxRanks * kMaxCtas * sizeof(uint32_t);
