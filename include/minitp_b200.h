@@ -243,11 +243,11 @@ int mtpb_set_decode_impl(int impl);
  * its stage events at [2048 + index]. */
 int mtpb_set_decode_trace(void* buf);
 
-/* Megakernel weight ring: at most `nslot_max` shared-memory slots of `slot_kb`
- * KiB, at most `inflight` bulk copies outstanding per CTA (0: up to the ring),
- * `l2_hint` != 0 streams weights with an L2 evict-first policy. Defaults
- * (8, 32, 2, 1). */
-int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint);
+/* Megakernel weight stream: chunks of at most `chunk_kb` KiB for the layers
+ * (default 96) and `lm_chunk_kb` KiB for the LM head (default 48), in a
+ * shared-memory ring that takes the rest of the block's shared memory;
+ * `l2_hint` != 0 (default) streams weights with an L2 evict-first policy. */
+int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_hint);
 
 /* Megakernel: nanoseconds a thread sleeps between two polls of a data word
  * that has not arrived yet (0, the default: poll back to back). */

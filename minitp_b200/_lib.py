@@ -104,7 +104,7 @@ SIGNATURES: dict[str, tuple] = {
                                        c_void_p, c_void_p]),
     "mtpb_set_decode_impl": (c_int, [c_int]),
     "mtpb_set_decode_trace": (c_int, [c_void_p]),
-    "mtpb_set_decode_ring": (c_int, [c_int, c_int, c_int, c_int]),
+    "mtpb_set_decode_ring": (c_int, [c_int, c_int, c_int]),
     "mtpb_set_decode_spin": (c_int, [c_int]),
 }
 

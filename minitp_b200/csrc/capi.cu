@@ -377,7 +377,7 @@ struct ModelHost {
 
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
-int g_mk_nslot_max = kMkMaxSlots, g_mk_slot_kb = 32, g_mk_inflight = 2, g_mk_l2hint = 1;
+int g_mk_slot_kb = 96, g_mk_lm_kb = 48, g_mk_l2hint = 1;
 uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
@@ -651,7 +651,7 @@ int smem_optin() {
 
 // Device scratch of the megakernel (LL words), sized for the largest batch.
 struct MkScratch {
-  size_t qkv, att, act, lm, total;
+  size_t qkv, att, head, act, lm, total;
 };
 
 MkScratch mk_scratch_layout(const mtpb_model_desc& d) {
@@ -661,9 +661,10 @@ MkScratch mk_scratch_layout(const mtpb_model_desc& d) {
   MkScratch s;
   s.qkv = up(size_t(kMkMaxM) * (nq / P) * 8);
   s.att = up(size_t(kMkMaxM) * d.hq_local * kMkMaxSplits * (d.head_dim + 2) * 8);
-  s.act = up(size_t(kMkMaxM) * (d.inter_local / P) * 8);
+  s.head = up(size_t(kMkRep) * kMkMaxM * (size_t(d.hq_local) * d.head_dim / P) * 8);
+  s.act = up(size_t(kMkRep) * kMkMaxM * (d.inter_local / P) * 8);
   s.lm = up(size_t(kMaxCtas) * kMkMaxM * 16);
-  s.total = s.qkv + s.att + s.act + s.lm;
+  s.total = s.qkv + s.att + s.head + s.act + s.lm;
   return s;
 }
 
@@ -681,11 +682,6 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   // 16-byte weight rows, and rows of whole LL pairs
   if (d.hidden % VE || d.inter_local % VE || (d.hq_local * hd) % VE) return kNotEligible;
   if (d.hidden % (2 * P) || d.inter_local % (2 * P)) return kNotEligible;
-  const size_t slot = size_t(g_mk_slot_kb) * 1024;
-  // one GEMV unit per ring slot at least: gate/up (2P rows of H), down (P rows of I), o_proj
-  if (size_t(2 * P) * d.hidden * tsz > slot || size_t(P) * d.inter_local * tsz > slot ||
-      size_t(P) * d.hq_local * hd * tsz > slot)
-    return kNotEligible;
   const int G = sm_count();
   if (G > kMaxCtas) return kNotEligible;
   const int ns = (cap + kMkSplit - 1) / kMkSplit;
@@ -703,26 +699,49 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   p.kv_cap = cap;
   p.nsplit = ns;
   p.xin_cols = std::max(d.hq_local * hd, d.inter_local);
-  p.wsc_floats = kMkCons * 3 * hd + 2 * M * d.hq_local * ns;
-  p.slot_bytes = int(slot);
-  // stage every attention item of a CTA when shared memory allows; the ring
-  // takes the rest (at least 2 slots)
+  p.wsc_floats = kMkCons * 3 * hd;
+  // every attention item of a CTA is staged in shared memory
   const int per_cta = (M * d.hq_local * ns + G - 1) / G;
-  const int budget = smem_optin() - 4096;  // static shared memory of the kernel
-  int stage = std::min(kMkMaxStage, per_cta);
-  int nslot = 0;
-  for (;;) {
-    p.att_stage = stage;
-    p.nslot = 0;
-    const size_t fixed = mk_layout(p, tsz).ring;
-    nslot = fixed < size_t(budget) ? int((size_t(budget) - fixed) / slot) : 0;
-    nslot = std::min(nslot, std::min(kMkMaxSlots, g_mk_nslot_max));
-    if (nslot >= 2 || stage == 0) break;
-    stage /= 2;
+  if (per_cta > kMkMaxStage) return kNotEligible;
+  p.att_stage = per_cta;
+  // stage kinds: units, their split over the CTAs, chunking
+  const size_t chunk_max = size_t(g_mk_slot_kb) * 1024;
+  const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * hd;
+  const size_t hvec = mk_align(size_t(d.hidden) * tsz);
+  struct KindShape {
+    int K, units, rpu, halves, hoff;
+    size_t pre;
+  };
+  const KindShape ks[kMkKinds] = {
+      {d.hidden, int(nq) / P, P, 1, 0, hvec + mk_align(nq * tsz)},  // QKV (+ ln1, bias)
+      {d.hq_local * hd, d.hidden / P, P, 1, 0, 0},                  // O
+      {d.hidden, d.inter_local / P, P, 2, d.inter_local, hvec},     // gate/up (+ ln2)
+      {d.inter_local, d.hidden / P, P, 1, 0, 0},                    // down
+      {d.hidden, int(d.vocab_end - d.vocab_start), 1, 1, 0, hvec},  // LM head (+ final norm)
+  };
+  size_t biggest = 0;
+  for (int k = 0; k < kMkKinds; ++k) {
+    MkKind& kd = p.kinds[k];
+    kd.K = ks[k].K;
+    kd.rpu = ks[k].rpu;
+    kd.halves = ks[k].halves;
+    kd.hoff = ks[k].hoff;
+    kd.base = ks[k].units / G;
+    kd.rem = ks[k].units % G;
+    kd.pre = int(ks[k].pre);
+    const size_t ub = size_t(kd.halves) * kd.rpu * kd.K * tsz;
+    // the LM head streams in smaller chunks: more of them in flight
+    const size_t cmax = k == kMkLm ? size_t(g_mk_lm_kb) * 1024 : chunk_max;
+    const size_t room = cmax > ks[k].pre ? cmax - ks[k].pre : 0;
+    kd.upc = int(std::max<size_t>(1, room / ub));
+    biggest = std::max(biggest, ks[k].pre + size_t(kd.upc) * ub);
   }
-  if (nslot < 2) return kNotEligible;
-  p.nslot = nslot;
-  p.inflight = std::min(g_mk_inflight, nslot - 1);
+  // the ring takes the rest of shared memory; it must hold the biggest chunk
+  const int budget = smem_optin() - 4096;  // static shared memory of the kernel
+  p.ring_bytes = 0;
+  const size_t fixed = mk_layout(p, tsz).ring;
+  if (fixed + biggest > size_t(budget)) return kNotEligible;
+  p.ring_bytes = int((size_t(budget) - fixed) & ~size_t(127));
   p.l2_hint = g_mk_l2hint;
   *smem_out = mk_layout(p, tsz).total;
   const MkScratch sl = mk_scratch_layout(d);
@@ -730,8 +749,9 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   char* s = mh.mk_scratch;
   p.qkv_ll = reinterpret_cast<uint64_t*>(s);
   p.att_ll = reinterpret_cast<uint64_t*>(s + sl.qkv);
-  p.act_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att);
-  p.lm_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att + sl.act);
+  p.head_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att);
+  p.act_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att + sl.head);
+  p.lm_ll = reinterpret_cast<uint64_t*>(s + sl.qkv + sl.att + sl.head + sl.act);
   return MTPB_OK;
 }
 
@@ -1208,12 +1228,11 @@ int mtpb_model_destroy(void* model) {
   return MTPB_OK;
 }
 
-int mtpb_set_decode_ring(int nslot_max, int slot_kb, int inflight, int l2_hint) {
-  if (nslot_max < 2 || nslot_max > kMkMaxSlots || slot_kb < 4 || slot_kb > 128 || slot_kb % 4 || inflight < 0)
-    return fail(MTPB_ERR_INVALID, "decode ring: 2 <= nslot <= 8, 4 <= slot_kb <= 128 (multiple of 4), inflight >= 0");
-  g_mk_nslot_max = nslot_max;
-  g_mk_slot_kb = slot_kb;
-  g_mk_inflight = inflight;
+int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_hint) {
+  if (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4 || lm_chunk_kb < 4 || lm_chunk_kb > 200 || lm_chunk_kb % 4)
+    return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4");
+  g_mk_slot_kb = chunk_kb;
+  g_mk_lm_kb = lm_chunk_kb;
   g_mk_l2hint = l2_hint ? 1 : 0;
   return MTPB_OK;
 }

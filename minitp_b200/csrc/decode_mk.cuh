@@ -3,10 +3,12 @@
 //
 // Warp 0 is a producer: one thread streams this CTA's slice of every weight
 // matrix of the step (QKV, O, gate/up and down of every layer, then the LM
-// head), in execution order, into a ring of shared-memory slots with 1-D bulk
-// copies (cp.async.bulk, no multicast) completing on mbarriers. Weights do not
-// depend on activations, so the stream runs ahead by up to `nslot` slots,
-// across stage and layer boundaries, while the consumers wait on data.
+// head), in execution order, into a circular byte ring in shared memory with
+// 1-D bulk copies (cp.async.bulk, no multicast) completing on mbarriers. Each
+// chunk is contiguous in the ring; the RMSNorm gains and the QKV bias travel
+// in front of the rows that follow them. Weights do not depend on
+// activations, so the stream runs ahead by the whole ring, across stage and
+// layer boundaries, while the consumers wait on data.
 //
 // Warps 1..15 consume. Per layer:
 //   QKV  : AllReduce site of the previous down projection (or the embedding):
@@ -31,10 +33,9 @@
 // {payload, sequence number} written by one aligned 64-bit store. Such a store
 // is single-copy atomic, so a reader (64-bit loads) that sees the expected
 // sequence number in a word also sees that word's payload; no memory fence
-// and no flag is needed.
-// Readers spin (bounded) on the words themselves. Sequence numbers grow with
-// the step counter, which every launch advances, so no word of an earlier
-// step or launch matches.
+// and no flag is needed. Readers spin (bounded) on the words themselves.
+// Sequence numbers grow with the step counter, which every launch advances,
+// so no word of an earlier step or launch matches.
 #pragma once
 
 #include <type_traits>
@@ -47,13 +48,19 @@ namespace mtpb {
 constexpr int kMkThreads = 512;
 constexpr int kMkCons = 15;  // consumer warps 1..15
 constexpr int kMkConsThreads = kMkCons * 32;
-constexpr int kMkMaxSlots = 8;
+constexpr int kMkRingSlots = 8;   // chunks in the ring at once (mbarrier pairs)
 constexpr int kMkMaxM = 8;
 constexpr int kMkSplit = 32;      // KV positions per attention item (one per lane)
-constexpr int kMkMaxSplits = 128;
-constexpr int kMkMaxStage = 16;   // attention items per CTA staged in shared memory
+constexpr int kMkMaxSplits = 64;  // the split merge holds two splits per lane
+constexpr int kMkMaxStage = 16;   // attention items per CTA (all staged in shared memory)
 constexpr int kMkChan = 2;        // communicator channel of the AllReduce sites
 constexpr int kMkHdr = 1024;      // shared-memory header: mbarriers + control words
+// Copies of the words that every CTA reads (merged attention output, act):
+// CTA b reads copy b % kMkRep, so fewer CTAs poll any one line.
+constexpr int kMkRep = 4;
+
+// GEMV stage kinds
+enum : int { kMkQkv = 0, kMkO = 1, kMkGu = 2, kMkDown = 3, kMkLm = 4, kMkKinds = 5 };
 
 // ---------------------------------------------------------------------------
 // LL words
@@ -111,6 +118,7 @@ __device__ __noinline__ LLSpin ll_spin_any(const uint64_t* src, uint32_t seq, in
   r.ok = 1;
   return r;
 }
+
 // T values per LL word and their packing (bf16: two values, low half first)
 template <typename T> struct LLPack;
 template <> struct LLPack<float> {
@@ -131,6 +139,29 @@ template <> struct LLPack<bf16> {
   }
 };
 
+// shared-memory loads by 32-bit shared address
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+template <typename T> __device__ __forceinline__ float lds_t(uint32_t a);
+template <> __device__ __forceinline__ float lds_t<float>(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+template <> __device__ __forceinline__ float lds_t<bf16>(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return __uint_as_float(uint32_t(v) << 16);
+}
+
 // ---------------------------------------------------------------------------
 // parameters
 // ---------------------------------------------------------------------------
@@ -144,6 +175,22 @@ struct MkLayer {
   const void* down_w;
   void* k_cache;
   void* v_cache;
+};
+
+// One GEMV stage kind, planned on the host. A unit is `rpu` consecutive rows
+// of each of `halves` row blocks (gate/up: unit u also takes rows
+// hoff + u * rpu ..), so a unit's outputs fill whole LL words. CTA b owns
+// units [b * base + min(b, rem), +base + (b < rem)); a chunk holds up to `upc`
+// units and, in front of the first chunk, `pre` bytes of vectors (gains, bias).
+struct MkKind {
+  int K;  // row length (elements)
+  int rpu;
+  int halves;
+  int hoff;
+  int base;
+  int rem;
+  int upc;
+  int pre;
 };
 
 struct MkParams {
@@ -166,25 +213,23 @@ struct MkParams {
   void* logits;
   uint64_t* qkv_ll;  // [M][nq / kPer] LL words
   uint64_t* att_ll;  // [items][hd + 2] LL words (fp32): o, then (max, sum)
-  uint64_t* act_ll;  // [M][I / kPer]
+  uint64_t* head_ll;  // [kMkRep][M][hq * hd / kPer] merged attention output
+  uint64_t* act_ll;   // [kMkRep][M][I / kPer]
   uint64_t* lm_ll;   // [CTA][kMkMaxM][2] packed argmax as two LL words
-  int nsplit;        // KV splits of the cache capacity (upper bound)
-  int att_stage;     // attention items per CTA staged in shared memory
-  int nslot;
-  int slot_bytes;
-  int inflight;  // max weight copies outstanding per CTA (0 = up to nslot)
-  int l2_hint;   // stream weights with an L2 evict-first policy
+  MkKind kinds[kMkKinds];
+  int nsplit;     // KV splits of the cache capacity (upper bound)
+  int att_stage;  // attention items per CTA (all staged in shared memory)
+  int ring_bytes;
+  int l2_hint;    // stream weights with an L2 evict-first policy
   int xin_cols;
-  int wsc_floats;  // kMkCons * 3 * hd (attention items) + 2 * M * hq * nsplit (split merge)
+  int wsc_floats;  // kMkCons * 3 * hd: q, new k and new v of each warp's attention item
   uint64_t budget_ns;
   uint32_t spin_ns;  // back-off between polls of a word that is not there yet
   // Optional stage timeline (%globaltimer ns): CTA 0 at [idx], the last CTA at
   // [2048 + idx], every CTA's layer-1 events at [4096 + e * 1024 + cta];
   // [0] start, [1 + 12 l + e] stage event e of layer l, then the LM head and
-  // selection events, [512 + s] CTA 0's first copy of weight stage s,
-  // [1000 ..] phases of CTA 0's first attention item, [1100 + 40 (s - 4) + 2 i]
-  // CTA 0's chunk i of layer-1 stage s ready / consumed, [1300 + 20 (s - 4) + i]
-  // its copy issued. NULL = off.
+  // selection events, [512 + s] CTA 0's first copy of stage s, [1000 ..]
+  // phases of CTA 0's first attention item. NULL = off.
   unsigned long long* trace;
 };
 
@@ -200,6 +245,59 @@ __device__ __forceinline__ bool ll_spin2(const MkParams& p, const uint64_t* src,
   const LLSpin r = ll_spin_any(src, seq, 1, p.budget_ns, abort, p.spin_ns);
   v = r.v;
   return r.ok != 0;
+}
+
+// Poll up to NB 16-byte LL pairs (or 8-byte words) until all carry seq.
+// Every round issues the loads of all that are still missing, so a round
+// costs one memory round trip however many are late. False on timeout or
+// abort.
+template <int NB, typename Addr>
+__device__ __forceinline__ bool ll_wait2(const MkParams& p, Addr addr, int n, uint32_t seq, uint4 (&v)[NB],
+                                         volatile int* abort) {
+  uint32_t pend = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+    if (b < n) v[b] = ll_ld2(addr(b));
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+    if (b < n && !ll_ok2(v[b], seq)) pend |= 1u << b;
+  if (!pend) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (p.spin_ns) __nanosleep(p.spin_ns);
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (pend & (1u << b)) v[b] = ll_ld2(addr(b));
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if ((pend & (1u << b)) && ll_ok2(v[b], seq)) pend &= ~(1u << b);
+    if (!pend) return true;
+    if ((it & 15) == 0 && (*abort || global_ns() - t0 > p.budget_ns)) return false;
+  }
+}
+template <int NB, typename Addr>
+__device__ __forceinline__ bool ll_wait1(const MkParams& p, Addr addr, int n, uint32_t seq, uint2 (&v)[NB],
+                                         volatile int* abort) {
+  uint32_t pend = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+    if (b < n) v[b] = ll_ld(addr(b));
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+    if (b < n && v[b].y != seq) pend |= 1u << b;
+  if (!pend) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (p.spin_ns) __nanosleep(p.spin_ns);
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (pend & (1u << b)) v[b] = ll_ld(addr(b));
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if ((pend & (1u << b)) && v[b].y == seq) pend &= ~(1u << b);
+    if (!pend) return true;
+    if ((it & 15) == 0 && (*abort || global_ns() - t0 > p.budget_ns)) return false;
+  }
 }
 
 #define MK_TRACE(c, p, idx)                                                                   \
@@ -238,77 +336,19 @@ __host__ __device__ inline MkLayout mk_layout(const MkParams& p, size_t tsz) {
   l.stg = off;
   off = mk_align(off + size_t(p.att_stage) * mk_stage_bytes(p, tsz));
   l.ring = off;
-  off = mk_align(off + size_t(p.nslot) * p.slot_bytes);
+  off = mk_align(off + size_t(p.ring_bytes));
   l.total = off;
   return l;
 }
 
-// Weight stage s (0 .. 4L): 4l+0 QKV, 4l+1 O, 4l+2 gate/up, 4l+3 down, 4L LM
-// head. A GEMV unit is `rpu` consecutive rows of each of `halves` row blocks
-// (gate/up: unit u takes gate rows u*rpu.. and up rows hoff + u*rpu..), so a
-// unit's outputs fill whole LL words.
-struct MkStage {
-  const char* w;
-  int K;  // row length (elements)
-  int units;
-  int rpu;
-  int halves;
-  int hoff;
-};
-
-template <typename T>
-__device__ __forceinline__ MkStage mk_stage(const MkParams& p, const MkLayer* lys, int s) {
-  constexpr int P = LLPack<T>::kPer;
-  MkStage st;
-  st.rpu = P;
-  st.halves = 1;
-  st.hoff = 0;
-  if (s == 4 * p.L) {
-    st.w = static_cast<const char*>(p.lm_head);
-    st.K = p.H;
-    st.units = int(p.vend - p.vstart);
-    st.rpu = 1;
-    return st;
-  }
-  const MkLayer& ly = lys[s >> 2];
-  switch (s & 3) {
-    case 0:
-      st.w = static_cast<const char*>(ly.qkv_w);
-      st.K = p.H;
-      st.units = (p.hq + 2 * p.hkv) * p.hd / P;
-      break;
-    case 1:
-      st.w = static_cast<const char*>(ly.o_w);
-      st.K = p.hq * p.hd;
-      st.units = p.H / P;
-      break;
-    case 2:
-      st.w = static_cast<const char*>(ly.gu_w);
-      st.K = p.H;
-      st.units = p.I / P;
-      st.halves = 2;
-      st.hoff = p.I;
-      break;
-    default:
-      st.w = static_cast<const char*>(ly.down_w);
-      st.K = p.I;
-      st.units = p.H / P;
-      break;
-  }
-  return st;
+__device__ __forceinline__ void mk_units(const MkKind& kd, int& u0, int& nu) {
+  const int b = blockIdx.x;
+  u0 = b * kd.base + min(b, kd.rem);
+  nu = kd.base + (b < kd.rem ? 1 : 0);
 }
 
-__device__ __forceinline__ void mk_part(int units, int& u0, int& nu) {
-  const int G = gridDim.x;
-  const int base = units / G, rem = units % G;
-  u0 = blockIdx.x * base + min(int(blockIdx.x), rem);
-  nu = base + (int(blockIdx.x) < rem ? 1 : 0);
-}
-
-__device__ __forceinline__ int mk_upc(const MkParams& p, const MkStage& st, size_t tsz) {
-  const int ub = st.halves * st.rpu * st.K * int(tsz);
-  return max(1, p.slot_bytes / ub);
-}
+// floor(kMkCons / n) for n = 0 .. 15
+__constant__ int kMkDivCons[16] = {1, 15, 7, 5, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 1, 1};
 
 // ---------------------------------------------------------------------------
 // consumer-side helpers (all kMkConsThreads consumer threads call them)
@@ -344,6 +384,7 @@ __device__ __forceinline__ float cons_sum(const MkCtx& c, float v) {
   if (c.lane == 0) c.red[c.cw] = v;
   cons_sync();
   float t = 0.f;
+#pragma unroll
   for (int i = 0; i < kMkCons; ++i) t += c.red[i];
   return t;
 }
@@ -370,30 +411,25 @@ __device__ __forceinline__ bool cons_reduce_norm(const MkCtx& c, const MkParams&
   for (int m = 0; m < p.M; ++m) {
     float ss = 0.f;
     for (int i = c.tid; i < nl && ok; i += kMkConsThreads) {
+      // the line of four ranks in flight together; summed in rank order
       float s[2 * P];
 #pragma unroll
       for (int e = 0; e < 2 * P; ++e) s[e] = 0.f;
-      // two ranks' pairs in flight at a time; summed in rank order
-      for (int r0 = 0; r0 < cm.world; r0 += 2) {
-        uint4 v[2];
+      for (int r0 = 0; r0 < cm.world; r0 += 4) {
+        uint4 v[4];
+        auto addr = [&](int r) { return mk_site(p, cm.rank, site, r0 + r) + size_t(m) * W + 2 * i; };
+        if (!ll_wait2<4>(p, addr, min(4, cm.world - r0), seq, v, c.abort)) ok = false;
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-          if (r0 + u < cm.world) v[u] = ll_ld2(mk_site(p, cm.rank, site, r0 + u) + size_t(m) * W + 2 * i);
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          if (r0 + u < cm.world && ok) {
-            if (!ll_ok2(v[u], seq) &&
-                !ll_spin2(p, mk_site(p, cm.rank, site, r0 + u) + size_t(m) * W + 2 * i, seq, v[u], c.abort))
-              ok = false;
+        for (int r = 0; r < 4; ++r) {
+          if (r0 + r < cm.world) {
             float f[2 * P];
-            LLPack<T>::unpack(v[u].x, f);
-            LLPack<T>::unpack(v[u].z, f + P);
+            LLPack<T>::unpack(v[r].x, f);
+            LLPack<T>::unpack(v[r].z, f + P);
 #pragma unroll
             for (int e = 0; e < 2 * P; ++e) s[e] += f[e];
           }
         }
       }
-      if (!ok) break;
 #pragma unroll
       for (int e = 0; e < 2 * P; ++e) {
         const size_t off = size_t(m) * H + size_t(i) * 2 * P + e;
@@ -419,26 +455,22 @@ template <typename T>
 __device__ __forceinline__ bool cons_gather(const MkCtx& c, const MkParams& p, const uint64_t* src, int n,
                                             uint32_t seq, T* dst, int ldd) {
   constexpr int P = LLPack<T>::kPer;
-  constexpr int NB = 4;
+  constexpr int NB = 3;
   const int nl = n / 2, tot = p.M * nl;
   bool ok = !*c.abort;
   for (int b0 = c.tid; b0 < tot && ok; b0 += NB * kMkConsThreads) {
     uint4 v[NB];
+    const int nb = min(NB, (tot - b0 + kMkConsThreads - 1) / kMkConsThreads);
+    auto addr = [&](int b) {
+      const int i = b0 + b * kMkConsThreads, m = i / nl, w = i - m * nl;
+      return src + size_t(m) * n + 2 * w;
+    };
+    if (!ll_wait2<NB>(p, addr, nb, seq, v, c.abort)) ok = false;
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const int i = b0 + b * kMkConsThreads;
-      if (i < tot) {
+      if (b < nb) {
         const int m = i / nl, w = i - m * nl;
-        v[b] = ll_ld2(src + size_t(m) * n + 2 * w);
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      const int i = b0 + b * kMkConsThreads;
-      if (i < tot && ok) {
-        const int m = i / nl, w = i - m * nl;
-        if (!ll_ok2(v[b], seq) && !ll_spin2(p, src + size_t(m) * n + 2 * w, seq, v[b], c.abort))
-          ok = false;
         float f[2 * P];
         LLPack<T>::unpack(v[b].x, f);
         LLPack<T>::unpack(v[b].z, f + P);
@@ -452,41 +484,81 @@ __device__ __forceinline__ bool cons_gather(const MkCtx& c, const MkParams& p, c
 }
 
 // ---------------------------------------------------------------------------
-// GEMV over one ring slot: n units of NR rows (RPU rows of NR / RPU halves).
-// x: [M][ldx] in shared memory. With fewer units than warps, K is split over
-// warps and the partial sums are added in a fixed order. ep(m, unit, v[NR]).
+// GEMV over one chunk: n units of NR rows (RPU rows of NR / RPU halves), the
+// row blocks starting at shared address `rows`, row length K. x: [M] rows of
+// `xstride` bytes at shared address `xs`. With fewer units than warps, K is
+// split over warps and the partial sums are added in a fixed order.
+// ep(m, unit, v[NR]).
 // ---------------------------------------------------------------------------
 template <typename T, int MT, int NR, int RPU, typename Ep>
-__device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, const char* slot, int n, int K, const T* x,
-                                                int ldx, int M, float* kred, Ep ep) {
+__device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, int n, int K, uint32_t xs,
+                                                int xstride, int M, float* kred, Ep ep) {
   constexpr int VE = VecTraits<T>::kElems;
   const int cpr = K / VE;
-  const size_t rb = size_t(K) * sizeof(T);
-  const int kp = n >= kMkCons ? 1 : max(1, min(kMkCons / n, cpr / 32));
+  const uint32_t rb = uint32_t(K) * sizeof(T);
+  // split K over warps only for long rows (more than 4 vectors per lane)
+  const int kp = n >= kMkCons ? 1 : max(1, min(kMkDivCons[n], (cpr + 127) >> 7));
   const int nw = n * kp;
   for (int w = c.cw; w < nw; w += kMkCons) {
-    const int j = w % n, q = w / n;
-    const char* rows[NR];
+    int j = w, q = 0;
+    if (kp > 1) {
+      while (j >= n) {
+        j -= n;
+        ++q;
+      }
+    }
+    uint32_t ra[NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) rows[r] = slot + (size_t((r / RPU) * n + j) * RPU + (r % RPU)) * rb;
+    for (int r = 0; r < NR; ++r) ra[r] = rows + uint32_t((r / RPU) * n * RPU + j * RPU + (r % RPU)) * rb;
     float acc[MT][NR];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
       for (int r = 0; r < NR; ++r) acc[m][r] = 0.f;
-    for (int k = q * 32 + c.lane; k < cpr; k += kp * 32) {
-      float wf[NR][VE];
+    // UN vectors per row in flight, then a remainder loop
+    constexpr int UN = NR >= 4 ? 2 : 4;
+    const int step = kp * 32;
+    int k = q * 32 + c.lane;
+    for (; k + (UN - 1) * step < cpr; k += UN * step) {
+      uint4 wv[UN][NR];
 #pragma unroll
-      for (int r = 0; r < NR; ++r) unpack(*reinterpret_cast<const uint4*>(rows[r] + size_t(k) * 16), wf[r]);
+      for (int u = 0; u < UN; ++u)
+#pragma unroll
+        for (int r = 0; r < NR; ++r) wv[u][r] = lds128(ra[r] + uint32_t(k + u * step) * 16);
+#pragma unroll
+      for (int u = 0; u < UN; ++u) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < M) {
+            float xf[VE];
+            unpack(lds128(xs + uint32_t(m * xstride) + uint32_t(k + u * step) * 16), xf);
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+              float wf[VE];
+              unpack(wv[u][r], wf);
+#pragma unroll
+              for (int e = 0; e < VE; ++e) acc[m][r] = fmaf(wf[e], xf[e], acc[m][r]);
+            }
+          }
+        }
+      }
+    }
+    for (; k < cpr; k += step) {
+      uint4 wv[NR];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) wv[r] = lds128(ra[r] + uint32_t(k) * 16);
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         if (m < M) {
           float xf[VE];
-          unpack(*reinterpret_cast<const uint4*>(x + size_t(m) * ldx + size_t(k) * VE), xf);
+          unpack(lds128(xs + uint32_t(m * xstride) + uint32_t(k) * 16), xf);
 #pragma unroll
-          for (int r = 0; r < NR; ++r)
+          for (int r = 0; r < NR; ++r) {
+            float wf[VE];
+            unpack(wv[r], wf);
 #pragma unroll
-            for (int e = 0; e < VE; ++e) acc[m][r] = fmaf(wf[r][e], xf[e], acc[m][r]);
+            for (int e = 0; e < VE; ++e) acc[m][r] = fmaf(wf[e], xf[e], acc[m][r]);
+          }
         }
       }
     }
@@ -508,15 +580,20 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, const char* slot
   }
   if (kp > 1) {
     cons_sync();
-    for (int i = c.tid; i < n * M; i += kMkConsThreads) {
-      const int j = i / M, m = i - j * M;
-      float v[NR];
+    if (c.tid < n) {
+      const int j = c.tid;
 #pragma unroll
-      for (int r = 0; r < NR; ++r) v[r] = 0.f;
-      for (int q = 0; q < kp; ++q)
+      for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+          float v[NR];
 #pragma unroll
-        for (int r = 0; r < NR; ++r) v[r] += kred[((j * kp + q) * kMkMaxM + m) * NR + r];
-      ep(m, j, v);
+          for (int r = 0; r < NR; ++r) v[r] = 0.f;
+          for (int q = 0; q < kp; ++q)
+#pragma unroll
+            for (int r = 0; r < NR; ++r) v[r] += kred[((j * kp + q) * kMkMaxM + m) * NR + r];
+          ep(m, j, v);
+        }
+      }
     }
     cons_sync();
   }
@@ -558,131 +635,134 @@ __device__ __forceinline__ void mk_stage_kv(const MkParams& p, const MkLayer& ly
   }
 }
 
-// One item. qs: 3 * hd floats of this warp. ks/vs: staged K/V rows of the
-// item (position p0 first), or NULL to read the cache in global memory.
-template <typename T>
+// One item, head_dim HD. qs: 3 * HD floats of this warp. ks/vs: the item's
+// staged K/V rows (position p0 first); the new position's row is filled in
+// here. Loops have compile-time trip counts and no branches inside, so the
+// shared-memory loads and shuffles of all positions are in flight together.
+template <typename T, int HD>
 __device__ __forceinline__ bool mk_att_item(const MkCtx& c, const MkParams& p, const MkLayer& ly, int it,
-                                            const MkItem& t, int pos, float* qs, const T* ks, const T* vs,
-                                            uint64_t* bar, uint32_t bar_par, uint32_t seq_in, uint32_t seq_out,
-                                            bool tr) {
+                                            const MkItem& t, int pos, float* qs, T* ks, T* vs, uint64_t* bar,
+                                            uint32_t bar_par, uint32_t seq_in, uint32_t seq_out, bool tr) {
   constexpr int P = LLPack<T>::kPer;
   constexpr int VE = VecTraits<T>::kElems;
-  const int hd = p.hd, half = hd >> 1, wph = hd / P;
-  const int nq = (p.hq + 2 * p.hkv) * hd;
+  constexpr int HALF = HD / 2, WPH = HD / P;     // LL words of one head
+  constexpr int NV = HD / VE;                    // 16-byte chunks of one K row
+  constexpr int ND = HD >= 32 ? HD / 32 : 1;     // PV dims per lane
+  const int nq = (p.hq + 2 * p.hkv) * HD;
   const bool has_new = pos >= t.p0 && pos < t.p1;
   const uint64_t* row = p.qkv_ll + size_t(t.m) * (nq / P);
-  const uint64_t* qw = row + size_t(t.h) * wph;
-  const uint64_t* kw = row + size_t(p.hq + t.kvh) * wph;
-  const uint64_t* vw = row + size_t(p.hq + p.hkv + t.kvh) * wph;
+  const uint64_t* qw = row + size_t(t.h) * WPH;
+  const uint64_t* kw = row + size_t(p.hq + t.kvh) * WPH;
+  const uint64_t* vw = row + size_t(p.hq + p.hkv + t.kvh) * WPH;
   float* q = qs;
-  float* kn = qs + hd;
-  float* vn = qs + 2 * hd;
+  float* kn = qs + HD;
+  float* vn = qs + 2 * HD;
   // q (and the new k, v) of this head: all loads first, then the spins
   bool ok = true;
-  for (int w = c.lane; w < wph; w += 32) {
-    uint2 a = ll_ld(qw + w), b = make_uint2(0, seq_in), d = make_uint2(0, seq_in);
+  for (int w = c.lane; w < WPH && ok; w += 32) {
+    uint2 v[3];
+    const uint64_t* src[3] = {qw + w, kw + w, vw + w};
+    auto addr = [&](int b) { return src[b]; };
+    if (!ll_wait1<3>(p, addr, has_new ? 3 : 1, seq_in, v, c.abort)) ok = false;
+    LLPack<T>::unpack(v[0].x, q + w * P);
     if (has_new) {
-      b = ll_ld(kw + w);
-      d = ll_ld(vw + w);
-    }
-    if (a.y != seq_in && !ll_spin(p, qw + w, seq_in, a, c.abort)) ok = false;
-    if (ok && b.y != seq_in && !ll_spin(p, kw + w, seq_in, b, c.abort)) ok = false;
-    if (ok && d.y != seq_in && !ll_spin(p, vw + w, seq_in, d, c.abort)) ok = false;
-    if (!ok) break;
-    LLPack<T>::unpack(a.x, q + w * P);
-    if (has_new) {
-      LLPack<T>::unpack(b.x, kn + w * P);
-      LLPack<T>::unpack(d.x, vn + w * P);
+      LLPack<T>::unpack(v[1].x, kn + w * P);
+      LLPack<T>::unpack(v[2].x, vn + w * P);
     }
   }
   if (!__all_sync(0xffffffffu, ok)) return false;
   __syncwarp();
   if (tr) p.trace[1000] = global_ns();
   // RoPE (reference rotate_half form, fp32 with T-rounded result), in place
-  const float* cs = p.cos_tab + size_t(pos) * hd;
-  const float* sn = p.sin_tab + size_t(pos) * hd;
-  for (int i = c.lane; i < half; i += 32) {
-    const float qa = q[i], qb = q[i + half];
+  const float* cs = p.cos_tab + size_t(pos) * HD;
+  const float* sn = p.sin_tab + size_t(pos) * HD;
+  for (int i = c.lane; i < HALF; i += 32) {
+    const float qa = q[i], qb = q[i + HALF];
     q[i] = round_t<T>(__fadd_rn(__fmul_rn(qa, cs[i]), __fmul_rn(-qb, sn[i])));
-    q[i + half] = round_t<T>(__fadd_rn(__fmul_rn(qb, cs[i + half]), __fmul_rn(qa, sn[i + half])));
+    q[i + HALF] = round_t<T>(__fadd_rn(__fmul_rn(qb, cs[i + HALF]), __fmul_rn(qa, sn[i + HALF])));
     if (has_new) {
-      const float ka = kn[i], kb = kn[i + half];
+      const float ka = kn[i], kb = kn[i + HALF];
       kn[i] = round_t<T>(__fadd_rn(__fmul_rn(ka, cs[i]), __fmul_rn(-kb, sn[i])));
-      kn[i + half] = round_t<T>(__fadd_rn(__fmul_rn(kb, cs[i + half]), __fmul_rn(ka, sn[i + half])));
+      kn[i + HALF] = round_t<T>(__fadd_rn(__fmul_rn(kb, cs[i + HALF]), __fmul_rn(ka, sn[i + HALF])));
     }
   }
   __syncwarp();
-  const size_t cbase = (size_t(t.m) * p.hkv + t.kvh) * p.kv_cap * hd;
-  T* kc = static_cast<T*>(ly.k_cache) + cbase;
-  T* vc = static_cast<T*>(ly.v_cache) + cbase;
-  // the first query head of the KV head stores the new K/V for later steps
-  if (has_new && t.h % (p.hq / p.hkv) == 0) {
-    for (int d = c.lane; d < hd; d += 32) {
-      kc[size_t(pos) * hd + d] = from_f<T>(kn[d]);
-      vc[size_t(pos) * hd + d] = from_f<T>(vn[d]);
-    }
-  }
-  if (bar && !__all_sync(0xffffffffu, mbar_wait(bar, bar_par, p.budget_ns, c.abort))) return false;
-  const T* kb = ks ? ks : kc + size_t(t.p0) * hd;
-  const T* vb = vs ? vs : vc + size_t(t.p0) * hd;
-  if (tr) p.trace[1001] = global_ns();
-  // scores: lane j takes position p0 + j; 16-byte chunks visited in a
-  // lane-rotated order so the lanes of a quarter warp hit distinct banks
-  const int NV = hd / VE;
-  const int j = c.lane, pp = t.p0 + j;
-  float s = -INFINITY;
-  if (pp < t.p1) {
-    float d = 0.f;
-    if (pp == pos) {
-      for (int e = 0; e < hd; ++e) d = fmaf(q[e], kn[e], d);
-    } else {
-      const T* kr = kb + size_t(j) * hd;
-      for (int v0 = 0; v0 < NV; v0 += 4) {
-        uint4 kv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (v0 + u < NV) kv[u] = ld_vec(kr + ((v0 + u + j) & (NV - 1)) * VE);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (v0 + u < NV) {
-            const float* qv = q + ((v0 + u + j) & (NV - 1)) * VE;
-            float kf[VE];
-            unpack(kv[u], kf);
-#pragma unroll
-            for (int e = 0; e < VE; ++e) d = fmaf(qv[e], kf[e], d);
-          }
-        }
+  if (has_new) {
+    // the new token's row joins the staged rows; the first query head of the
+    // KV head also stores it in the cache for later steps
+    const int jn = pos - t.p0;
+    const bool store = t.h % (p.hq / p.hkv) == 0;
+    T* kc = static_cast<T*>(ly.k_cache) + ((size_t(t.m) * p.hkv + t.kvh) * p.kv_cap + pos) * HD;
+    T* vc = static_cast<T*>(ly.v_cache) + ((size_t(t.m) * p.hkv + t.kvh) * p.kv_cap + pos) * HD;
+    for (int d = c.lane; d < HD; d += 32) {
+      const T kv = from_f<T>(kn[d]), vv = from_f<T>(vn[d]);
+      ks[size_t(jn) * HD + d] = kv;
+      vs[size_t(jn) * HD + d] = vv;
+      if (store) {
+        kc[d] = kv;
+        vc[d] = vv;
       }
     }
-    s = d * p.scale;
   }
+  if (!__all_sync(0xffffffffu, mbar_wait(bar, bar_par, p.budget_ns, c.abort))) return false;
+  __syncwarp();
+  if (tr) p.trace[1001] = global_ns();
+  // scores: lane j takes position p0 + j (lanes past the split read row 0 and
+  // are masked afterwards); 16-byte chunks visited in a lane-rotated order so
+  // the lanes of a quarter warp hit distinct banks
+  const int nt = t.p1 - t.p0;
+  const int j = c.lane;
+  const int jr = j < nt ? j : 0;
+  const uint32_t ks_s = smem_u32(ks), vs_s = smem_u32(vs), q_s = smem_u32(q);
+  float d4[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const uint32_t kr = ks_s + uint32_t(jr * HD) * sizeof(T);
+    uint4 kv[NV];
+#pragma unroll
+    for (int u = 0; u < NV; ++u) kv[u] = lds128(kr + uint32_t((u + j) & (NV - 1)) * 16);
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+      const uint32_t qa = q_s + uint32_t(((u + j) & (NV - 1)) * VE) * 4;
+      float qf[VE], kf[VE];
+#pragma unroll
+      for (int e = 0; e < VE; e += 4) {
+        const float4 f = lds128f(qa + e * 4);
+        qf[e] = f.x;
+        qf[e + 1] = f.y;
+        qf[e + 2] = f.z;
+        qf[e + 3] = f.w;
+      }
+      unpack(kv[u], kf);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) d4[e & 3] = fmaf(qf[e], kf[e], d4[e & 3]);
+    }
+  }
+  const float s = j < nt ? ((d4[0] + d4[1]) + (d4[2] + d4[3])) * p.scale : -INFINITY;
   float mx = s;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  const float pl = pp < t.p1 ? expf(s - mx) : 0.f;
+  const float pl = j < nt ? expf(s - mx) : 0.f;
   const float l = warp_sum(pl);
   if (tr) p.trace[1002] = global_ns();
-  // PV: lane owns dims lane, lane + 32, ...
-  float o[4] = {0.f, 0.f, 0.f, 0.f};
-  const int nt = t.p1 - t.p0;
-#pragma unroll 4
-  for (int jj = 0; jj < nt; ++jj) {
+  // PV: lane owns dims lane + 32 i; positions past the split have weight 0
+  // and read row 0, so the loop runs without branches
+  float o[ND];
+#pragma unroll
+  for (int i = 0; i < ND; ++i) o[i] = 0.f;
+  const int dl = HD >= 32 ? c.lane : (c.lane & (HD - 1));
+#pragma unroll
+  for (int jj = 0; jj < kMkSplit; ++jj) {
     const float pj = __shfl_sync(0xffffffffu, pl, jj);
-    const bool isnew = t.p0 + jj == pos;
-    const T* vr = vb + size_t(jj) * hd;
+    const uint32_t vr = vs_s + uint32_t((jj < nt ? jj : 0) * HD) * sizeof(T);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int d = c.lane + 32 * i;
-      if (d < hd) o[i] = fmaf(pj, isnew ? vn[d] : to_f(vr[d]), o[i]);
-    }
+    for (int i = 0; i < ND; ++i) o[i] = fmaf(pj, lds_t<T>(vr + uint32_t(dl + 32 * i) * sizeof(T)), o[i]);
   }
-  uint64_t* dst = p.att_ll + size_t(it) * (hd + 2);
+  uint64_t* dst = p.att_ll + size_t(it) * (HD + 2);
+  if (HD >= 32 || c.lane < HD) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int d = c.lane + 32 * i;
-    if (d < hd) ll_put(dst + d, __float_as_uint(o[i]), seq_out);
+    for (int i = 0; i < ND; ++i) ll_put(dst + dl + 32 * i, __float_as_uint(o[i]), seq_out);
   }
-  if (c.lane == 0) ll_put2(dst + hd, __float_as_uint(mx), __float_as_uint(l), seq_out);
+  if (c.lane == 0) ll_put2(dst + HD, __float_as_uint(mx), __float_as_uint(l), seq_out);
   if (tr) p.trace[1003] = global_ns();
   return true;
 }
@@ -697,12 +777,13 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
   __shared__ float kred[kMkCons * kMkMaxM * 4];
   __shared__ long long bests[kMkCons][kMkMaxM];
   __shared__ long long cta_best[kMkMaxM];
+  __shared__ int ring_lo[kMkRingSlots], ring_hi[kMkRingSlots];  // ring range of a chunk in flight
   constexpr int P = LLPack<T>::kPer;
   const size_t tsz = sizeof(T);
   const MkLayout lay = mk_layout(p, tsz);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kMkMaxSlots;
-  uint64_t* sbar = empty + kMkMaxSlots;  // [kMkMaxStage] attention staging
+  uint64_t* empty = full + kMkRingSlots;
+  uint64_t* sbar = empty + kMkRingSlots;  // [kMkMaxStage] attention staging
   volatile int* abort = reinterpret_cast<volatile int*>(sbar + kMkMaxStage);
   int* never = const_cast<int*>(abort) + 1;  // stays 0: "no abort" for the final drains
   MkLayer* lys = reinterpret_cast<MkLayer*>(smem + lay.lys);
@@ -719,7 +800,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
   const int pos = *reinterpret_cast<volatile int*>(p.pos_ptr);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.nslot; ++s) {
+    for (int s = 0; s < kMkRingSlots; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, kMkCons);
     }
@@ -739,59 +820,91 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
   }
   __syncthreads();
   const uint32_t nsite = uint32_t(2 * p.L + 2);
-  const uint32_t nloc = uint32_t(3 * p.L + 1);
+  // local sequence numbers: 4l qkv, 4l+1 attention partials, 4l+2 merged
+  // attention output, 4l+3 act; 4L the LM winners
+  const uint32_t nloc = uint32_t(4 * p.L + 1);
   auto site_seq = [&](int site) { return step * nsite + uint32_t(site) + 1u; };
   auto loc_seq = [&](int k) { return step * nloc + uint32_t(k) + 1u; };
-  const int nstages = 4 * p.L + 1;
+  const int H = p.H;
+  const int nq = (p.hq + 2 * p.hkv) * p.hd;
+  const uint32_t hvec = uint32_t(mk_align(size_t(H) * tsz));  // a gain vector in front of a chunk
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int k = 0;
+      int k = 0, k_old = 0, head = 0;
       bool stop = *abort != 0;
       const uint64_t pol = l2_evict_first_policy();
-      for (int s = 0; s < nstages && !stop; ++s) {
-        const MkStage st = mk_stage<T>(p, lys, s);
+      for (int s = 0; s < 4 * p.L + 1 && !stop; ++s) {
+        const int kind = s == 4 * p.L ? int(kMkLm) : (s & 3);
+        const MkKind& kd = p.kinds[kind];
+        const MkLayer* ly = kind == kMkLm ? nullptr : lys + (s >> 2);
+        const void* wv = kind == kMkQkv ? ly->qkv_w
+                         : kind == kMkO ? ly->o_w
+                         : kind == kMkGu ? ly->gu_w
+                         : kind == kMkDown ? ly->down_w
+                                           : p.lm_head;
+        const char* w = static_cast<const char*>(wv);
         int u0, nu;
-        mk_part(st.units, u0, nu);
-        const int upc = mk_upc(p, st, tsz);
-        const size_t rb = size_t(st.K) * tsz, ub = size_t(st.rpu) * rb;
-        for (int c = 0; c < nu; c += upc, ++k) {
-          const int n = min(upc, nu - c);
-          const int slot = k % p.nslot;
-          if (k >= p.nslot && !mbar_wait(empty + slot, ((k / p.nslot) - 1) & 1, p.budget_ns, abort)) {
-            *abort = 1;
-            atomicOr(p.comm.status(), kStatusTimeout);
+        mk_units(kd, u0, nu);
+        const uint32_t rb = uint32_t(kd.K) * uint32_t(tsz), hb1 = uint32_t(kd.rpu) * rb;
+        // a stage with vectors in front has at least one chunk, even without units
+        for (int cc = 0; (cc < nu || (cc == 0 && kd.pre)) && !stop; cc += kd.upc) {
+          const int n = max(0, min(kd.upc, nu - cc));
+          const uint32_t pre = cc == 0 ? uint32_t(kd.pre) : 0u;
+          const uint32_t B = pre + uint32_t(kd.halves * n) * hb1;
+          const int at = head + int(B) <= p.ring_bytes ? head : 0;
+          // room: fewer than kMkRingSlots chunks in flight, none overlapping [at, at + B)
+          for (;;) {
+            bool fit = k - k_old < kMkRingSlots;
+            for (int i = k_old; i < k && fit; ++i)
+              fit = at + int(B) <= ring_lo[i & (kMkRingSlots - 1)] || at >= ring_hi[i & (kMkRingSlots - 1)];
+            if (fit) break;
+            if (!mbar_wait(empty + (k_old & (kMkRingSlots - 1)), uint32_t(k_old / kMkRingSlots) & 1u, p.budget_ns,
+                           abort)) {
+              *abort = 1;
+              atomicOr(p.comm.status(), kStatusTimeout);
+              stop = true;
+              break;
+            }
+            ++k_old;
+          }
+          if (stop || *abort) {
             stop = true;
             break;
           }
-          // at most `inflight` copies outstanding
-          if (p.inflight > 0 && k >= p.inflight) {
-            const int kk = k - p.inflight;
-            mbar_wait(full + (kk % p.nslot), (kk / p.nslot) & 1, p.budget_ns, abort);
+          const int slot = k & (kMkRingSlots - 1);
+          ring_lo[slot] = at;
+          ring_hi[slot] = at + int(B);
+          char* dst = ring + at;
+          // exact transaction bytes: the vectors in front, then the rows
+          uint32_t tx = uint32_t(kd.halves * n) * hb1;
+          const void* v0 = nullptr;
+          const void* v1 = nullptr;
+          if (pre) {
+            v0 = kind == kMkQkv ? ly->ln1 : kind == kMkGu ? ly->ln2 : p.final_norm;
+            v1 = kind == kMkQkv ? ly->qkv_b : nullptr;
+            tx += uint32_t(H) * uint32_t(tsz) + (v1 ? uint32_t(nq) * uint32_t(tsz) : 0u);
           }
-          if (*abort) {
-            stop = true;
-            break;
-          }
-          char* dst = ring + size_t(slot) * p.slot_bytes;
-          const uint32_t hb = uint32_t(n * ub);
-          if (c == 0 && p.trace && blockIdx.x == 0) p.trace[512 + s] = global_ns();
-          if (p.trace && blockIdx.x == 0 && s >= 4 && s < 8 && c / upc < 20) p.trace[1300 + (s - 4) * 20 + c / upc] = global_ns();
-          mbar_arrive_expect_tx(full + slot, hb * st.halves);
-          for (int h = 0; h < st.halves; ++h) {
-            const char* src = st.w + (size_t(h) * st.hoff + size_t(u0 + c) * st.rpu) * rb;
+          if (p.trace && blockIdx.x == 0 && cc == 0) p.trace[512 + s] = global_ns();
+          mbar_arrive_expect_tx(full + slot, tx);
+          if (v0) bulk_g2s(dst, v0, uint32_t(H) * uint32_t(tsz), full + slot);
+          if (v1) bulk_g2s(dst + hvec, v1, uint32_t(nq) * uint32_t(tsz), full + slot);
+          for (int h = 0; h < kd.halves; ++h) {
+            const char* src = w + (size_t(h) * kd.hoff + size_t(u0 + cc) * kd.rpu) * rb;
+            char* d = dst + pre + uint32_t(h * n) * hb1;
             if (p.l2_hint)
-              bulk_g2s_hint(dst + size_t(h) * hb, src, hb, full + slot, pol);
+              bulk_g2s_hint(d, src, uint32_t(n) * hb1, full + slot, pol);
             else
-              bulk_g2s(dst + size_t(h) * hb, src, hb, full + slot);
+              bulk_g2s(d, src, uint32_t(n) * hb1, full + slot);
           }
+          head = at + int(B);
+          ++k;
         }
       }
       // drain: the copies in flight must land before the CTA exits
-      const int issued = k;
-      for (int i = max(0, issued - p.nslot); i < issued; ++i)
-        mbar_wait(full + (i % p.nslot), (i / p.nslot) & 1, p.budget_ns, never);
+      for (int i = max(0, k - kMkRingSlots); i < k; ++i)
+        mbar_wait(full + (i & (kMkRingSlots - 1)), uint32_t(i / kMkRingSlots) & 1u, p.budget_ns, never);
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -803,50 +916,56 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     c.abort = abort;
     const Comm& cm = p.comm;
     const int G = gridDim.x;
-    int k = 0;  // chunk counter (matches the producer)
+    const uint32_t ring_s = smem_u32(ring);
+    int kc = 0;  // chunk counter (matches the producer)
 
-    // consume every chunk of weight stage s; x: [M][ldx] in shared memory
-    auto run_stage = [&](int s, const T* x, int ldx, auto nr_tag, auto rpu_tag, auto ep) {
+    // wait for the next chunk; its offset in the ring
+    auto chunk_wait = [&]() -> uint32_t {
+      const int slot = kc & (kMkRingSlots - 1);
+      if (!mbar_wait(full + slot, uint32_t(kc / kMkRingSlots) & 1u, p.budget_ns, abort) && !*abort) mk_fail(c, p);
+      return uint32_t(ring_lo[slot]);
+    };
+    auto chunk_release = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + (kc & (kMkRingSlots - 1)));
+      ++kc;
+    };
+    // GEMV of every chunk of a stage kind; the first chunk may already be
+    // waited for (first >= 0: its ring offset). x: [M][ldx] T in shared memory
+    auto run_kind = [&](int kind, int first, const T* x, int ldx, auto nr_tag, auto rpu_tag, auto ep) {
       constexpr int NR = decltype(nr_tag)::value;
       constexpr int RPU = decltype(rpu_tag)::value;
-      const MkStage st = mk_stage<T>(p, lys, s);
+      const MkKind& kd = p.kinds[kind];
       int u0, nu;
-      mk_part(st.units, u0, nu);
-      const int upc = mk_upc(p, st, tsz);
-      for (int cc = 0; cc < nu; cc += upc, ++k) {
-        const int n = min(upc, nu - cc);
-        const int slot = k % p.nslot;
-        const char* sl = ring + size_t(slot) * p.slot_bytes;
-        if (!mbar_wait(full + slot, (k / p.nslot) & 1, p.budget_ns, abort)) {
-          if (!*abort) mk_fail(c, p);
-        }
-        const bool trc = p.trace && blockIdx.x == 0 && c.tid == 0 && s >= 4 && s < 8 && cc / upc < 20;
-        if (trc) p.trace[1100 + (s - 4) * 40 + 2 * (cc / upc)] = global_ns();
+      mk_units(kd, u0, nu);
+      for (int cc = 0; cc < nu || (cc == 0 && kd.pre); cc += kd.upc) {
+        const int n = max(0, min(kd.upc, nu - cc));
+        const uint32_t off = (cc == 0 && first >= 0) ? uint32_t(first) : chunk_wait();
+        const uint32_t pre = cc == 0 ? uint32_t(kd.pre) : 0u;
         // every consumer runs the chunk (it may synchronise the consumers);
         // after an abort the outputs are dropped
         auto epu = [&](int m, int j, const float* v) {
           if (!*abort) ep(m, u0 + cc + j, v);
         };
-        cons_gemv_chunk<T, MT, NR, RPU>(c, sl, n, st.K, x, ldx, p.M, kred, epu);
-        if (trc) p.trace[1101 + (s - 4) * 40 + 2 * (cc / upc)] = global_ns();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + slot);
+        cons_gemv_chunk<T, MT, NR, RPU>(c, ring_s + off + pre, n, kd.K, smem_u32(x), ldx * int(tsz), p.M, kred,
+                                        epu);
+        chunk_release();
       }
     };
     using I1 = std::integral_constant<int, 1>;
     using IP = std::integral_constant<int, P>;
     using I2P = std::integral_constant<int, 2 * P>;
 
-    // attention items of this CTA: it = blockIdx.x + G * li, warp li % kMkCons;
-    // the first att_stage local items have their K/V staged in shared memory
+    // attention items of this CTA: it = blockIdx.x + G * li, warp li % kMkCons,
+    // K/V staged in shared memory slot li
     const int nsp = min(p.nsplit, (pos + kMkSplit) / kMkSplit);
     const int n_items = p.M * p.hq * nsp;
-    const int n_loc = blockIdx.x < n_items ? (n_items - 1 - int(blockIdx.x)) / G + 1 : 0;
+    const int n_loc = min(p.att_stage, int(blockIdx.x) < n_items ? (n_items - 1 - int(blockIdx.x)) / G + 1 : 0);
     const size_t stg_elems = mk_stage_bytes(p, tsz) / tsz;
     float* qs = wsc + size_t(c.cw) * 3 * p.hd;
     auto stage_layer = [&](int l) {
       if (lane == 0) {
-        for (int li = c.cw; li < min(n_loc, p.att_stage); li += kMkCons) {
+        for (int li = c.cw; li < n_loc; li += kMkCons) {
           const int it = blockIdx.x + G * li;
           T* ks = stg + size_t(li) * stg_elems;
           mk_stage_kv<T>(p, lys[l], mk_item(p, it, nsp, pos), pos, ks, ks + stg_elems / 2, sbar + li);
@@ -862,10 +981,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     MK_TRACE(c, p, 0);
     bool alive = !cons_sync_or(*abort != 0);
     // ---- embedding -> site 0 (this CTA's word slice of every row)
+    const int WH = H / P;
     if (alive) {
-      const int W = p.H / P;
-      int w0, nw;
-      mk_part(W, w0, nw);
+      const int base = WH / G, rem = WH % G;
+      const int w0 = blockIdx.x * base + min(int(blockIdx.x), rem), nw = base + (int(blockIdx.x) < rem ? 1 : 0);
       const uint32_t seq = site_seq(0);
       for (int i = c.tid; i < p.M * nw; i += kMkConsThreads) {
         const int m = i / nw, w = w0 + (i - m * nw);
@@ -875,32 +994,32 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         float f[P];
 #pragma unroll
         for (int e = 0; e < P; ++e)
-          f[e] = mine ? to_f(static_cast<const T*>(p.embed)[size_t(id - p.vstart) * p.H + size_t(w) * P + e]) : 0.f;
+          f[e] = mine ? to_f(static_cast<const T*>(p.embed)[size_t(id - p.vstart) * H + size_t(w) * P + e]) : 0.f;
         const uint32_t u = LLPack<T>::pack(f);
-        for (int d = 0; d < cm.world; ++d) ll_put(mk_site(p, d, 0, cm.rank) + size_t(m) * W + w, u, seq);
+        for (int d = 0; d < cm.world; ++d) ll_put(mk_site(p, d, 0, cm.rank) + size_t(m) * WH + w, u, seq);
       }
     }
-    const int nq = (p.hq + 2 * p.hkv) * p.hd;
-    const int WH = p.H / P;
 
     for (int l = 0; l < p.L && alive; ++l) {
       const MkLayer& ly = lys[l];
       const int tb = 1 + 12 * l;
       MK_TRACE(c, p, tb + 0);
-      // ---- QKV
-      alive = cons_reduce_norm<T>(c, p, 2 * l, site_seq(2 * l), l > 0, static_cast<const T*>(ly.ln1), xres, xnorm);
-      if (!alive) break;
-      MK_TRACE(c, p, tb + 1);
+      // ---- QKV (its first chunk carries ln1 and the bias)
       {
-        const T* bias = static_cast<const T*>(ly.qkv_b);
+        const uint32_t off = chunk_wait();
+        const T* gain = reinterpret_cast<const T*>(ring + off);
+        const T* bias = ly.qkv_b ? reinterpret_cast<const T*>(ring + off + hvec) : nullptr;
+        alive = cons_reduce_norm<T>(c, p, 2 * l, site_seq(2 * l), l > 0, gain, xres, xnorm);
+        MK_TRACE(c, p, tb + 1);
         uint64_t* out = p.qkv_ll;
-        const uint32_t seq = loc_seq(3 * l);
-        run_stage(4 * l, xnorm, p.H, IP{}, IP{}, [&](int m, int u, const float* v) {
+        const uint32_t seq = loc_seq(4 * l);
+        run_kind(kMkQkv, int(off), xnorm, H, IP{}, IP{}, [&](int m, int u, const float* v) {
           float r[P];
 #pragma unroll
           for (int e = 0; e < P; ++e) r[e] = bias ? v[e] + to_f(bias[u * P + e]) : v[e];
           ll_put(out + size_t(m) * (nq / P) + u, LLPack<T>::pack(r), seq);
         });
+        if (!alive) break;
       }
       MK_TRACE(c, p, tb + 2);
       // ---- attention items
@@ -908,11 +1027,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         bool ok = true;
         for (int li = c.cw; li < n_loc && ok; li += kMkCons) {
           const int it = blockIdx.x + G * li;
-          const bool st = li < p.att_stage;
-          const T* ks = st ? stg + size_t(li) * stg_elems : nullptr;
-          ok = mk_att_item<T>(c, p, ly, it, mk_item(p, it, nsp, pos), pos, qs, ks, st ? ks + stg_elems / 2 : nullptr,
-                              st ? sbar + li : nullptr, uint32_t(l & 1), loc_seq(3 * l), loc_seq(3 * l + 1),
-                              p.trace && blockIdx.x == 0 && li == 0);
+          T* ks = stg + size_t(li) * stg_elems;
+          const MkItem t = mk_item(p, it, nsp, pos);
+          const bool tr = p.trace && blockIdx.x == 0 && li == 0;
+          const uint32_t sp = uint32_t(l & 1), si = loc_seq(4 * l), so = loc_seq(4 * l + 1);
+          T* vs = ks + stg_elems / 2;
+          switch (p.hd) {
+            case 16: ok = mk_att_item<T, 16>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+            case 32: ok = mk_att_item<T, 32>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+            case 64: ok = mk_att_item<T, 64>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+            default: ok = mk_att_item<T, 128>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+          }
           __syncwarp();
         }
         if (!ok && lane == 0 && !*abort) mk_fail(c, p);
@@ -924,21 +1049,76 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         }
         MK_TRACE(c, p, tb + 4);
       }
-      // ---- O: merge the splits of every (row, head) into xin
+      // ---- O: (row, head) pair pr is merged by warp (pr / G) % kMkCons of CTA
+      // pr % G, which publishes the head's output; every CTA then gathers the
+      // merged outputs into xin. The merging warp holds split s (and s + 32)
+      // in lane s: w_s = exp(m_s - max) / sum_s exp(m_s - max) l_s.
       {
-        const int hd = p.hd, pairs = p.M * p.hq, npart = pairs * nsp;
-        const uint32_t seq = loc_seq(3 * l + 1);
-        // after the per-warp attention scratch: a warp of this CTA may still be
-        // in its item while other threads already collect the partials
-        float* msc = wsc + size_t(kMkCons) * 3 * hd;  // [pairs][nsp]: split max, then merge weight
-        float* lsc = msc + npart;                      // [pairs][nsp]: split sum
+        const int hd = p.hd, hd2 = hd / 2, pairs = p.M * p.hq;
+        const uint32_t seq = loc_seq(4 * l + 1), hseq = loc_seq(4 * l + 2);
+        const size_t head_n = size_t(p.M) * (p.hq * hd / P);
         bool ok = !*abort;
-        for (int i = c.tid; i < npart && ok; i += kMkConsThreads) {
-          const uint64_t* a = p.att_ll + size_t(i) * (hd + 2) + hd;
-          uint4 v = ll_ld2(a);
-          if (!ll_ok2(v, seq) && !ll_spin2(p, a, seq, v, abort)) ok = false;
-          msc[i] = __uint_as_float(v.x);
-          lsc[i] = __uint_as_float(v.z);
+        for (int pr = blockIdx.x + G * c.cw; pr < pairs && ok; pr += G * kMkCons) {
+          const uint64_t* part = p.att_ll + size_t(pr) * nsp * (hd + 2);
+          uint4 a[2];
+          a[0] = make_uint4(__float_as_uint(-INFINITY), seq, 0u, seq);
+          a[1] = a[0];
+          {
+            const int na = lane + 32 < nsp ? 2 : lane < nsp ? 1 : 0;
+            auto addr = [&](int b) { return part + size_t(lane + 32 * b) * (hd + 2) + hd; };
+            if (!ll_wait2<2>(p, addr, na, seq, a, abort)) ok = false;
+          }
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          const uint4 a0 = a[0], a1 = a[1];
+          const float m0 = __uint_as_float(a0.x), m1 = __uint_as_float(a1.x);
+          float mx = fmaxf(m0, m1);
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          float w0 = m0 == -INFINITY ? 0.f : expf(m0 - mx), w1 = m1 == -INFINITY ? 0.f : expf(m1 - mx);
+          const float den = warp_sum(fmaf(w0, __uint_as_float(a0.z), w1 * __uint_as_float(a1.z)));
+          const float inv = 1.0f / den;
+          w0 *= inv;
+          w1 *= inv;
+          const int m = pr / p.hq, hh = pr - m * p.hq;
+          // every lane runs every iteration (the shuffles need the whole warp);
+          // lanes past the head's dim pairs load and store nothing
+          for (int dp0 = 0; dp0 < hd2; dp0 += 32) {
+            const int dp = dp0 + lane;
+            const bool act = dp < hd2;
+            float o[2] = {0.f, 0.f};
+            for (int s0 = 0; s0 < nsp; s0 += 4) {
+              uint4 v[4];
+              auto addr = [&](int u) { return part + size_t(s0 + u) * (hd + 2) + 2 * dp; };
+              if (act && ok && !ll_wait2<4>(p, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int sidx = s0 + u;
+                if (sidx < nsp) {
+                  const float ws = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
+                  if (act) {
+                    o[0] = fmaf(ws, __uint_as_float(v[u].x), o[0]);
+                    o[1] = fmaf(ws, __uint_as_float(v[u].z), o[1]);
+                  }
+                }
+              }
+            }
+            if (act && !*abort) {
+              // dims (2 dp, 2 dp + 1) of head hh: word (hh * hd + 2 dp) / P
+              const size_t w = size_t(m) * (p.hq * hd / P) + (size_t(hh) * hd + 2 * dp) / P;
+#pragma unroll
+              for (int r = 0; r < kMkRep; ++r) {
+                uint64_t* dst = p.head_ll + r * head_n + w;
+                if constexpr (P == 2) {
+                  ll_put(dst, LLPack<T>::pack(o), hseq);
+                } else {
+                  ll_put2(dst, __float_as_uint(o[0]), __float_as_uint(o[1]), hseq);
+                }
+              }
+            }
+          }
         }
         if (!ok && !*abort) mk_fail(c, p);
         if (cons_sync_or(!ok || *abort)) {
@@ -946,57 +1126,13 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
           break;
         }
         MK_TRACE(c, p, tb + 5);
-        // weights w_s = exp(m_s - max) / sum_s exp(m_s - max) l_s
-        for (int pr = c.tid; pr < pairs; pr += kMkConsThreads) {
-          float* ms = msc + size_t(pr) * nsp;
-          const float* ls = lsc + size_t(pr) * nsp;
-          float mx = -INFINITY;
-          for (int s = 0; s < nsp; ++s) mx = fmaxf(mx, ms[s]);
-          float den = 0.f;
-          for (int s = 0; s < nsp; ++s) {
-            const float w = ms[s] == -INFINITY ? 0.f : expf(ms[s] - mx);
-            ms[s] = w;
-            den = fmaf(w, ls[s], den);
-          }
-          const float inv = 1.0f / den;
-          for (int s = 0; s < nsp; ++s) ms[s] *= inv;
-        }
-        cons_sync();
-        const int hd2 = hd / 2;
-        for (int i = c.tid; i < pairs * hd2 && ok; i += kMkConsThreads) {
-          const int pr = i / hd2, d = 2 * (i - pr * hd2);
-          const uint64_t* base = p.att_ll + size_t(pr) * nsp * (hd + 2) + d;
-          const float* w = msc + size_t(pr) * nsp;
-          float a0 = 0.f, a1 = 0.f;
-          for (int s0 = 0; s0 < nsp && ok; s0 += 4) {
-            uint4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (s0 + u < nsp) v[u] = ll_ld2(base + size_t(s0 + u) * (hd + 2));
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              if (s0 + u < nsp && ok) {
-                if (!ll_ok2(v[u], seq) &&
-                    !ll_spin2(p, base + size_t(s0 + u) * (hd + 2), seq, v[u], abort))
-                  ok = false;
-                a0 = fmaf(w[s0 + u], __uint_as_float(v[u].x), a0);
-                a1 = fmaf(w[s0 + u], __uint_as_float(v[u].z), a1);
-              }
-            }
-          }
-          const int m = pr / p.hq, col = (pr - m * p.hq) * hd + d;
-          xin[size_t(m) * p.xin_cols + col] = from_f<T>(a0);
-          xin[size_t(m) * p.xin_cols + col + 1] = from_f<T>(a1);
-        }
-        if (!ok && !*abort) mk_fail(c, p);
-        if (cons_sync_or(!ok || *abort)) {
-          alive = false;
-          break;
-        }
+        alive = cons_gather<T>(c, p, p.head_ll + (blockIdx.x % kMkRep) * head_n, p.hq * hd / P, hseq, xin,
+                               p.xin_cols);
+        if (!alive) break;
         MK_TRACE(c, p, tb + 6);
         // o_proj -> site 2l+1 of every rank
         const uint32_t sseq = site_seq(2 * l + 1);
-        run_stage(4 * l + 1, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
+        run_kind(kMkO, -1, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
           float r[P];
 #pragma unroll
           for (int e = 0; e < P; ++e) r[e] = round_t<T>(v[e]);
@@ -1005,32 +1141,37 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         });
       }
       MK_TRACE(c, p, tb + 7);
-      // ---- GU
-      alive = cons_reduce_norm<T>(c, p, 2 * l + 1, site_seq(2 * l + 1), true, static_cast<const T*>(ly.ln2), xres,
-                                  xnorm);
-      if (!alive) break;
-      MK_TRACE(c, p, tb + 8);
+      // ---- GU (its first chunk carries ln2)
       {
+        const uint32_t off = chunk_wait();
+        const T* gain = reinterpret_cast<const T*>(ring + off);
+        alive = cons_reduce_norm<T>(c, p, 2 * l + 1, site_seq(2 * l + 1), true, gain, xres, xnorm);
+        MK_TRACE(c, p, tb + 8);
         uint64_t* act = p.act_ll;
-        const uint32_t seq = loc_seq(3 * l + 2);
-        run_stage(4 * l + 2, xnorm, p.H, I2P{}, IP{}, [&](int m, int u, const float* v) {
+        const size_t act_n = size_t(p.M) * (p.I / P);
+        const uint32_t seq = loc_seq(4 * l + 3);
+        run_kind(kMkGu, int(off), xnorm, H, I2P{}, IP{}, [&](int m, int u, const float* v) {
           float a[P];
 #pragma unroll
           for (int e = 0; e < P; ++e) {
             const float gr = round_t<T>(v[e]), ur = round_t<T>(v[P + e]);
             a[e] = round_t<T>(gr / (1.0f + expf(-gr))) * ur;
           }
-          ll_put(act + size_t(m) * (p.I / P) + u, LLPack<T>::pack(a), seq);
+          const uint32_t wd = LLPack<T>::pack(a);
+#pragma unroll
+          for (int r = 0; r < kMkRep; ++r) ll_put(act + r * act_n + size_t(m) * (p.I / P) + u, wd, seq);
         });
+        if (!alive) break;
       }
       MK_TRACE(c, p, tb + 9);
       // ---- DOWN
-      alive = cons_gather<T>(c, p, p.act_ll, p.I / P, loc_seq(3 * l + 2), xin, p.xin_cols);
+      alive = cons_gather<T>(c, p, p.act_ll + (blockIdx.x % kMkRep) * size_t(p.M) * (p.I / P), p.I / P,
+                             loc_seq(4 * l + 3), xin, p.xin_cols);
       if (!alive) break;
       MK_TRACE(c, p, tb + 10);
       {
         const uint32_t sseq = site_seq(2 * l + 2);
-        run_stage(4 * l + 3, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
+        run_kind(kMkDown, -1, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
           float r[P];
 #pragma unroll
           for (int e = 0; e < P; ++e) r[e] = round_t<T>(v[e]);
@@ -1041,11 +1182,11 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
       MK_TRACE(c, p, tb + 11);
     }
 
-    // ---- final norm + LM head + packed argmax
-    if (alive)
-      alive = cons_reduce_norm<T>(c, p, 2 * p.L, site_seq(2 * p.L), true, static_cast<const T*>(p.final_norm), xres,
-                                  xnorm);
+    // ---- final norm + LM head + packed argmax (the first LM chunk carries the gain)
     if (alive) {
+      const uint32_t off = chunk_wait();
+      const T* gain = reinterpret_cast<const T*>(ring + off);
+      alive = cons_reduce_norm<T>(c, p, 2 * p.L, site_seq(2 * p.L), true, gain, xres, xnorm);
       MK_TRACE(c, p, 1 + 12 * p.L);
       long long best[kMkMaxM];
 #pragma unroll
@@ -1053,7 +1194,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
       const bool nan_wins = cm.world == 1;
       const int vloc = int(p.vend - p.vstart);
       T* lg = static_cast<T*>(p.logits);
-      run_stage(4 * p.L, xnorm, p.H, I1{}, I1{}, [&](int m, int u, const float* v) {
+      run_kind(kMkLm, int(off), xnorm, H, I1{}, I1{}, [&](int m, int u, const float* v) {
         const float x = round_t<T>(v[0]);
         if (lg) lg[size_t(m) * vloc + u] = from_f<T>(x);
         const long long pk = argmax_pack(x, uint32_t(p.vstart) + uint32_t(u), nan_wins);
@@ -1067,8 +1208,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         if (lane == 0) bests[c.cw][m] = b;
       }
       cons_sync();
-      const uint32_t lseq = loc_seq(3 * p.L);
-      if (c.tid < p.M) {
+      const uint32_t lseq = loc_seq(4 * p.L);
+      if (alive && c.tid < p.M) {
         long long b = kArgmaxEmpty;
         for (int w = 0; w < kMkCons; ++w) b = bests[w][c.tid] > b ? bests[w][c.tid] : b;
         const unsigned long long ub = static_cast<unsigned long long>(b);
@@ -1077,7 +1218,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         if (c.tid == 0 && p.trace && blockIdx.x == 0) p.trace[2 + 12 * p.L] = global_ns();
       }
       // ---- CTA 0: best over CTAs, then over ranks; token write, advance
-      if (blockIdx.x == 0) {
+      if (alive && blockIdx.x == 0) {
         cons_sync();
         bool ok = !*abort;
         for (int i = c.tid; i < G * p.M && ok; i += kMkConsThreads) {
@@ -1131,7 +1272,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     }
     // bulk copies into this warp's staging buffers must land before exit
     if (lane == 0 && staged_layer >= 0) {
-      for (int li = c.cw; li < min(n_loc, p.att_stage); li += kMkCons)
+      for (int li = c.cw; li < n_loc; li += kMkCons)
         mbar_wait(sbar + li, uint32_t(staged_layer & 1), p.budget_ns, never);
     }
   }
