@@ -23,6 +23,7 @@ Reported (rank 0, one JSON line):
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -152,13 +153,16 @@ def kv_bytes_per_token(model, batch: int, avg_len: float) -> float:
     return per_pos * avg_len * batch * len(model.model.layers)
 
 
-def launches_per_generation(n_layers: int, new_tokens: int, prefill_tokens: int) -> int:
-    """minitp_b200 kernel launches of one fixed-length generation."""
+def launches_per_generation(n_layers: int, new_tokens: int, prefill_tokens: int, step_launches: int) -> int:
+    """minitp_b200 kernel launches of one fixed-length generation.
+
+    Prefill runs the kernel chain; every decode step makes `step_launches`
+    launches (1 when the decode megakernel runs it, as the library reports).
+    """
     prefill = 1 + n_layers * 5 + (2 * n_layers + 1 if prefill_tokens > 1 else 0) + 1
     select = 2  # argmax rows + finish
     seed = 1  # decode position store
-    step = 1 + 5 * n_layers + 1 + 1
-    return prefill + select + seed + (new_tokens - 1) * step
+    return prefill + select + seed + (new_tokens - 1) * step_launches
 
 
 # ---------------------------------------------------------------------- #
@@ -311,7 +315,12 @@ def run_b200(args, cfg, prompt_len, new_tokens):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = args.batch * new_tokens / (te.item() / 1e3)
 
-    # dominant kernel, timed live: the LM-head GEMV over this rank's vocab shard
+    # decode launches per step as the library plans them (1 = megakernel)
+    nk = ctypes.c_int(0)
+    _lib.call("mtpb_model_decode_kernels", model.native(), args.batch, prompt_len + new_tokens, ctypes.byref(nk))
+    step_launches = nk.value
+
+    # the prefill GEMV, timed live: the LM-head weights over this rank's vocab shard
     x = torch.randn(args.batch, cfg.hidden_size, device=dev).to(dtype)
     w = model.lm_head.weight
     for _ in range(3):
@@ -348,20 +357,25 @@ def run_b200(args, cfg, prompt_len, new_tokens):
                 "model": args.model, "global_batch": args.batch, "seq_len": prompt_len + new_tokens,
                 "parallelism": f"tp{world}", "heads_padded": bool(model.cfg.is_padded),
                 "l2": "flushed between timed steps (256 MiB write)",
-                "decode": "CUDA graph replay of the device-resident decode step, PDL chained kernels",
+                "decode": "CUDA graph replay of the device-resident decode step (persistent megakernel)",
             },
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
                     "d2h_bytes_per_step": args.batch * (prompt_len + new_tokens) * 8,
                     "definition": "generate_greedy from pinned host ids to host output ids, incl. prefill"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel (LM head, vocab shard)",
-                         "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(k_gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                         "bytes_per_launch": k_bytes, "us_per_launch": round(k_ms * 1e3, 3)},
-            "roofline_token": {"bound": "hbm", "achieved": round(tok_gbs, 1), "peak": peak, "unit": "GB/s",
-                               "frac": round(tok_gbs / peak, 4), "weight_bytes": wb, "kv_bytes": round(kvb),
-                               "peak_kind": peak_kind},
-            "gpu_launches": launches_per_generation(cfg.num_hidden_layers, new_tokens, prompt_len) * args.steps,
+            "roofline": {"bound": "hbm",
+                         "kernel": "decode_mk_kernel" if step_launches == 1 else "decode kernel chain",
+                         "achieved": round(tok_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(tok_gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_launch": round(wb + kvb), "weight_bytes": wb, "kv_bytes": round(kvb),
+                         "us_per_launch": round(ms_per_token * 1e3, 3),
+                         "timing": "CUDA events over the graph replays of the decode step (one launch each)"},
+            "roofline_gemv": {"bound": "hbm", "kernel": "gemv_kernel (LM-head weights, prefill GEMV)",
+                              "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(k_gbs / peak, 4), "bytes_per_launch": k_bytes,
+                              "us_per_launch": round(k_ms * 1e3, 3)},
+            "gpu_launches": launches_per_generation(cfg.num_hidden_layers, new_tokens, prompt_len,
+                                                    step_launches) * args.steps,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -230,6 +230,11 @@ int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_cach
                            void* const* v_caches, int cap, int64_t* out_ids, int ld_out,
                            void* logits, void* stream);
 
+/* Number of kernel launches one mtpb_model_decode_step makes for B rows and
+ * cache capacity `cap` with the current implementation setting (1 when the
+ * megakernel runs it). */
+int mtpb_model_decode_kernels(void* model, int B, int cap, int* launches);
+
 /* Decode-step implementation: 0 (default) = the persistent megakernel (one
  * cooperative launch per token; used when B <= 8 and the shapes fit its
  * shared-memory plan), 1 = the chain of per-operation kernels. */

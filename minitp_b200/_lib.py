@@ -102,6 +102,7 @@ SIGNATURES: dict[str, tuple] = {
                                    c_void_p, c_int, c_void_p]),
     "mtpb_model_decode_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int,
                                        c_void_p, c_void_p]),
+    "mtpb_model_decode_kernels": (c_int, [c_void_p, c_int, c_int, POINTER(c_int)]),
     "mtpb_set_decode_impl": (c_int, [c_int]),
     "mtpb_set_decode_trace": (c_int, [c_void_p]),
     "mtpb_set_decode_ring": (c_int, [c_int, c_int, c_int]),

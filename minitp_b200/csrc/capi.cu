@@ -1275,6 +1275,21 @@ int mtpb_model_forward(void* model, const int64_t* ids, int B, int T, const int6
   return model_forward(*mh, a, static_cast<cudaStream_t>(stream));
 }
 
+int mtpb_model_decode_kernels(void* model, int B, int cap, int* launches) {
+  if (!model || !launches || B <= 0 || cap <= 0) return fail(MTPB_ERR_INVALID, "model_decode_kernels: bad argument");
+  auto* mh = static_cast<ModelHost*>(model);
+  int mk = 0;
+  if (g_decode_impl == 0) {
+    MTPB_TRY(mk_reserve(*mh));
+    MkParams p;
+    size_t smem = 0;
+    mk = mk_plan(*mh, B, cap, p, &smem) == MTPB_OK ? 1 : 0;
+  }
+  // kernel chain: embedding, 5 per layer, final AllReduce + norm, LM head, argmax finish
+  *launches = mk ? 1 : 1 + 5 * mh->d.n_layers + 2;
+  return MTPB_OK;
+}
+
 int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_caches, void* const* v_caches, int cap,
                            int64_t* out_ids, int ld_out, void* logits, void* stream) {
   if (!model || !tok || !k_caches || !v_caches) return fail(MTPB_ERR_INVALID, "model_decode_step: null argument");
