@@ -250,9 +250,10 @@ int mtpb_set_decode_trace(void* buf);
 
 /* Megakernel weight stream: chunks of at most `chunk_kb` KiB for the layers
  * (default 96) and `lm_chunk_kb` KiB for the LM head (default 48), in a
- * shared-memory ring that takes the rest of the block's shared memory;
- * `l2_hint` != 0 (default) streams weights with an L2 evict-first policy. */
-int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_hint);
+ * shared-memory ring that takes the rest of the block's shared memory.
+ * `l2_flags` bit 0: stream weights with an L2 evict-first policy; bit 1:
+ * prefetch the next layer's weight rows into L2 (default 3, both). */
+int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags);
 
 /* Megakernel: nanoseconds a thread sleeps between two polls of a data word
  * that has not arrived yet (0, the default: poll back to back). */

@@ -377,7 +377,7 @@ struct ModelHost {
 
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
-int g_mk_slot_kb = 96, g_mk_lm_kb = 48, g_mk_l2hint = 1;
+int g_mk_slot_kb = 96, g_mk_lm_kb = 48, g_mk_l2hint = 1, g_mk_l2ahead = 1;
 uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
@@ -743,6 +743,7 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   if (fixed + biggest > size_t(budget)) return kNotEligible;
   p.ring_bytes = int((size_t(budget) - fixed) & ~size_t(127));
   p.l2_hint = g_mk_l2hint;
+  p.l2_ahead = g_mk_l2ahead;
   *smem_out = mk_layout(p, tsz).total;
   const MkScratch sl = mk_scratch_layout(d);
   if (mh.mk_bytes < sl.total) return kNotEligible;  // reserved by mk_reserve
@@ -1228,12 +1229,14 @@ int mtpb_model_destroy(void* model) {
   return MTPB_OK;
 }
 
-int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_hint) {
+int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
   if (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4 || lm_chunk_kb < 4 || lm_chunk_kb > 200 || lm_chunk_kb % 4)
     return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4");
+  if (l2_flags < 0 || l2_flags > 3) return fail(MTPB_ERR_INVALID, "decode ring: l2 flags 0..3");
   g_mk_slot_kb = chunk_kb;
   g_mk_lm_kb = lm_chunk_kb;
-  g_mk_l2hint = l2_hint ? 1 : 0;
+  g_mk_l2hint = l2_flags & 1;
+  g_mk_l2ahead = (l2_flags >> 1) & 1;
   return MTPB_OK;
 }
 

@@ -221,6 +221,7 @@ struct MkParams {
   int att_stage;  // attention items per CTA (all staged in shared memory)
   int ring_bytes;
   int l2_hint;    // stream weights with an L2 evict-first policy
+  int l2_ahead;   // prefetch the next layer's weight rows into L2
   int xin_cols;
   int wsc_floats;  // kMkCons * 3 * hd: q, new k and new v of each warp's attention item
   uint64_t budget_ns;
@@ -229,7 +230,8 @@ struct MkParams {
   // [2048 + idx], every CTA's layer-1 events at [4096 + e * 1024 + cta];
   // [0] start, [1 + 12 l + e] stage event e of layer l, then the LM head and
   // selection events, [512 + s] CTA 0's first copy of stage s, [1000 ..]
-  // phases of CTA 0's first attention item. NULL = off.
+  // phases of CTA 0's first attention item, [1100], [1101] CTA 0's SM clock
+  // (clock64) at its start and end, [1102] the time at its end. NULL = off.
   unsigned long long* trace;
 };
 
@@ -358,6 +360,7 @@ struct MkCtx {
   int cw;   // consumer warp 0..14
   int lane;
   float* red;
+  float* kred;  // split-K partial sums of the GEMV chunks
   volatile int* abort;
 };
 
@@ -491,11 +494,14 @@ __device__ __forceinline__ bool cons_gather(const MkCtx& c, const MkParams& p, c
 // ep(m, unit, v[NR]).
 // ---------------------------------------------------------------------------
 template <typename T, int MT, int NR, int RPU, typename Ep>
-__device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, int n, int K, uint32_t xs,
+__device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, const char* rows, int n, int K, const char* xs,
                                                 int xstride, int M, float* kred, Ep ep) {
   constexpr int VE = VecTraits<T>::kElems;
   const int cpr = K / VE;
   const uint32_t rb = uint32_t(K) * sizeof(T);
+  // plain loads through pointers into the shared-memory array: the compiler
+  // sees their address space and schedules them freely
+  auto ld16 = [](const char* a) { return *reinterpret_cast<const uint4*>(a); };
   // split K over warps only for long rows (more than 4 vectors per lane)
   const int kp = n >= kMkCons ? 1 : max(1, min(kMkDivCons[n], (cpr + 127) >> 7));
   const int nw = n * kp;
@@ -507,9 +513,9 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, i
         ++q;
       }
     }
-    uint32_t ra[NR];
+    const char* ra[NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) ra[r] = rows + uint32_t((r / RPU) * n * RPU + j * RPU + (r % RPU)) * rb;
+    for (int r = 0; r < NR; ++r) ra[r] = rows + size_t((r / RPU) * n * RPU + j * RPU + (r % RPU)) * rb;
     float acc[MT][NR];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
@@ -524,14 +530,14 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, i
 #pragma unroll
       for (int u = 0; u < UN; ++u)
 #pragma unroll
-        for (int r = 0; r < NR; ++r) wv[u][r] = lds128(ra[r] + uint32_t(k + u * step) * 16);
+        for (int r = 0; r < NR; ++r) wv[u][r] = ld16(ra[r] + size_t(k + u * step) * 16);
 #pragma unroll
       for (int u = 0; u < UN; ++u) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           if (m < M) {
             float xf[VE];
-            unpack(lds128(xs + uint32_t(m * xstride) + uint32_t(k + u * step) * 16), xf);
+            unpack(ld16(xs + size_t(m) * xstride + size_t(k + u * step) * 16), xf);
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
               float wf[VE];
@@ -546,12 +552,12 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, i
     for (; k < cpr; k += step) {
       uint4 wv[NR];
 #pragma unroll
-      for (int r = 0; r < NR; ++r) wv[r] = lds128(ra[r] + uint32_t(k) * 16);
+      for (int r = 0; r < NR; ++r) wv[r] = ld16(ra[r] + size_t(k) * 16);
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         if (m < M) {
           float xf[VE];
-          unpack(lds128(xs + uint32_t(m * xstride) + uint32_t(k) * 16), xf);
+          unpack(ld16(xs + size_t(m) * xstride + size_t(k) * 16), xf);
 #pragma unroll
           for (int r = 0; r < NR; ++r) {
             float wf[VE];
@@ -597,6 +603,52 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, uint32_t rows, i
     }
     cons_sync();
   }
+}
+
+// Epilogue of a layer's GEMV stage: what happens to the outputs of unit u.
+struct MkEpi {
+  int kind;         // kMkQkv, kMkO, kMkGu or kMkDown
+  uint32_t seq;     // sequence number of the words it writes
+  int site;         // AllReduce site (O, down)
+  const void* bias; // QKV bias (shared memory) or null
+};
+
+// One chunk of a layer's GEMV stage with its epilogue (QKV, O and down share
+// the NR = kPer code, gate/up has its own).
+template <typename T, int MT, int NR, int RPU>
+__device__ __forceinline__ void mk_stage_chunk(MkCtx c, const MkParams& p, MkEpi e, const char* rows, int n, int K,
+                                            const char* xs, int xstride, int u_base) {
+  constexpr int P = LLPack<T>::kPer;
+  const Comm& cm = p.comm;
+  auto ep = [&](int m, int j, const float* v) {
+    if (*c.abort) return;
+    const int u = u_base + j;
+    float r[P];
+    if (e.kind == kMkGu) {
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const float gr = round_t<T>(v[k]), ur = round_t<T>(v[(P + k) % NR]);
+        r[k] = round_t<T>(gr / (1.0f + expf(-gr))) * ur;
+      }
+      const uint32_t wd = LLPack<T>::pack(r);
+      const size_t act_n = size_t(p.M) * (p.I / P);
+#pragma unroll
+      for (int q = 0; q < kMkRep; ++q) ll_put(p.act_ll + q * act_n + size_t(m) * (p.I / P) + u, wd, e.seq);
+    } else if (e.kind == kMkQkv) {
+      const T* bias = static_cast<const T*>(e.bias);
+#pragma unroll
+      for (int k = 0; k < P; ++k) r[k] = bias ? v[k] + to_f(bias[u * P + k]) : v[k];
+      const int nq = (p.hq + 2 * p.hkv) * p.hd;
+      ll_put(p.qkv_ll + size_t(m) * (nq / P) + u, LLPack<T>::pack(r), e.seq);
+    } else {
+#pragma unroll
+      for (int k = 0; k < P; ++k) r[k] = round_t<T>(v[k]);
+      const uint32_t wd = LLPack<T>::pack(r);
+      const int WH = p.H / P;
+      for (int d = 0; d < cm.world; ++d) ll_put(mk_site(p, d, e.site, cm.rank) + size_t(m) * WH + u, wd, e.seq);
+    }
+  };
+  cons_gemv_chunk<T, MT, NR, RPU>(c, rows, n, K, xs, xstride, p.M, c.kred, ep);
 }
 
 // ---------------------------------------------------------------------------
@@ -897,6 +949,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
               bulk_g2s_hint(d, src, uint32_t(n) * hb1, full + slot, pol);
             else
               bulk_g2s(d, src, uint32_t(n) * hb1, full + slot);
+            // the same rows of the next layer start moving into L2 now, so its
+            // ring copies are L2 hits
+            if (p.l2_ahead && n > 0 && s + 4 < 4 * p.L) {
+              const MkLayer* ln = lys + (s >> 2) + 1;
+              const void* wn = kind == kMkQkv ? ln->qkv_w
+                               : kind == kMkO ? ln->o_w
+                               : kind == kMkGu ? ln->gu_w
+                                               : ln->down_w;
+              bulk_prefetch_l2(static_cast<const char*>(wn) + (size_t(h) * kd.hoff + size_t(u0 + cc) * kd.rpu) * rb,
+                               uint32_t(n) * hb1);
+            }
           }
           head = at + int(B);
           ++k;
@@ -913,10 +976,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     c.cw = warp - 1;
     c.lane = lane;
     c.red = red;
+    c.kred = kred;
     c.abort = abort;
     const Comm& cm = p.comm;
     const int G = gridDim.x;
-    const uint32_t ring_s = smem_u32(ring);
     int kc = 0;  // chunk counter (matches the producer)
 
     // wait for the next chunk; its offset in the ring
@@ -932,6 +995,22 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     };
     // GEMV of every chunk of a stage kind; the first chunk may already be
     // waited for (first >= 0: its ring offset). x: [M][ldx] T in shared memory
+    auto run_stage = [&](int kind, int first, const T* x, int ldx, MkEpi e) {
+      const MkKind& kd = p.kinds[kind];
+      int u0, nu;
+      mk_units(kd, u0, nu);
+      for (int cc = 0; cc < nu || (cc == 0 && kd.pre); cc += kd.upc) {
+        const int n = max(0, min(kd.upc, nu - cc));
+        const uint32_t off = (cc == 0 && first >= 0) ? uint32_t(first) : chunk_wait();
+        const uint32_t pre = cc == 0 ? uint32_t(kd.pre) : 0u;
+        const char* xr = reinterpret_cast<const char*>(x);
+        if (kind == kMkGu)
+          mk_stage_chunk<T, MT, 2 * P, P>(c, p, e, ring + off + pre, n, kd.K, xr, ldx * int(tsz), u0 + cc);
+        else
+          mk_stage_chunk<T, MT, P, P>(c, p, e, ring + off + pre, n, kd.K, xr, ldx * int(tsz), u0 + cc);
+        chunk_release();
+      }
+    };
     auto run_kind = [&](int kind, int first, const T* x, int ldx, auto nr_tag, auto rpu_tag, auto ep) {
       constexpr int NR = decltype(nr_tag)::value;
       constexpr int RPU = decltype(rpu_tag)::value;
@@ -947,8 +1026,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
         auto epu = [&](int m, int j, const float* v) {
           if (!*abort) ep(m, u0 + cc + j, v);
         };
-        cons_gemv_chunk<T, MT, NR, RPU>(c, ring_s + off + pre, n, kd.K, smem_u32(x), ldx * int(tsz), p.M, kred,
-                                        epu);
+        cons_gemv_chunk<T, MT, NR, RPU>(c, ring + off + pre, n, kd.K, reinterpret_cast<const char*>(x),
+                                        ldx * int(tsz), p.M, kred, epu);
         chunk_release();
       }
     };
@@ -979,6 +1058,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     }
 
     MK_TRACE(c, p, 0);
+    if (p.trace && blockIdx.x == 0 && c.tid == 0) p.trace[1100] = clock64();
     bool alive = !cons_sync_or(*abort != 0);
     // ---- embedding -> site 0 (this CTA's word slice of every row)
     const int WH = H / P;
@@ -1000,186 +1080,143 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
       }
     }
 
-    for (int l = 0; l < p.L && alive; ++l) {
+    // The layers as a sequence of phases; each kind of phase (reduce + norm,
+    // GEMV stage, gather, attention, merge) appears once in the code and
+    // serves every place of a layer that needs it, which keeps the code a
+    // layer executes small. Phases k of layer l:
+    //   0 reduce (site 2l) + ln1    1 QKV     2 attention   3 merge
+    //   4 gather head outputs       5 O       6 reduce (site 2l+1) + ln2
+    //   7 gate/up                   8 gather act             9 down
+    uint32_t first_off = 0;   // ring offset of the chunk that carries the gain
+    const T* qkv_bias = nullptr;
+    for (int ph = 0; ph < 10 * p.L && alive; ++ph) {
+      const int l = ph / 10, k = ph - 10 * l;
       const MkLayer& ly = lys[l];
       const int tb = 1 + 12 * l;
-      MK_TRACE(c, p, tb + 0);
-      // ---- QKV (its first chunk carries ln1 and the bias)
-      {
-        const uint32_t off = chunk_wait();
-        const T* gain = reinterpret_cast<const T*>(ring + off);
-        const T* bias = ly.qkv_b ? reinterpret_cast<const T*>(ring + off + hvec) : nullptr;
-        alive = cons_reduce_norm<T>(c, p, 2 * l, site_seq(2 * l), l > 0, gain, xres, xnorm);
-        MK_TRACE(c, p, tb + 1);
-        uint64_t* out = p.qkv_ll;
-        const uint32_t seq = loc_seq(4 * l);
-        run_kind(kMkQkv, int(off), xnorm, H, IP{}, IP{}, [&](int m, int u, const float* v) {
-          float r[P];
-#pragma unroll
-          for (int e = 0; e < P; ++e) r[e] = bias ? v[e] + to_f(bias[u * P + e]) : v[e];
-          ll_put(out + size_t(m) * (nq / P) + u, LLPack<T>::pack(r), seq);
-        });
-        if (!alive) break;
-      }
-      MK_TRACE(c, p, tb + 2);
-      // ---- attention items
-      {
-        bool ok = true;
-        for (int li = c.cw; li < n_loc && ok; li += kMkCons) {
-          const int it = blockIdx.x + G * li;
-          T* ks = stg + size_t(li) * stg_elems;
-          const MkItem t = mk_item(p, it, nsp, pos);
-          const bool tr = p.trace && blockIdx.x == 0 && li == 0;
-          const uint32_t sp = uint32_t(l & 1), si = loc_seq(4 * l), so = loc_seq(4 * l + 1);
-          T* vs = ks + stg_elems / 2;
-          switch (p.hd) {
-            case 16: ok = mk_att_item<T, 16>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-            case 32: ok = mk_att_item<T, 32>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-            case 64: ok = mk_att_item<T, 64>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-            default: ok = mk_att_item<T, 128>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+      if (k == 0 || k == 6) {
+        if (k == 0) MK_TRACE(c, p, tb + 0);
+        first_off = chunk_wait();
+        const T* gain = reinterpret_cast<const T*>(ring + first_off);
+        if (k == 0) qkv_bias = ly.qkv_b ? reinterpret_cast<const T*>(ring + first_off + hvec) : nullptr;
+        const int site = 2 * l + (k == 6 ? 1 : 0);
+        alive = cons_reduce_norm<T>(c, p, site, site_seq(site), k == 6 || l > 0, gain, xres, xnorm);
+        MK_TRACE(c, p, tb + (k == 0 ? 1 : 8));
+      } else if (k == 1 || k == 5 || k == 7 || k == 9) {
+        const int kind = k == 1 ? int(kMkQkv) : k == 5 ? int(kMkO) : k == 7 ? int(kMkGu) : int(kMkDown);
+        const bool from_norm = kind == kMkQkv || kind == kMkGu;
+        MkEpi e;
+        e.kind = kind;
+        e.site = kind == kMkO ? 2 * l + 1 : 2 * l + 2;
+        e.seq = kind == kMkQkv ? loc_seq(4 * l) : kind == kMkGu ? loc_seq(4 * l + 3) : site_seq(e.site);
+        e.bias = kind == kMkQkv ? qkv_bias : nullptr;
+        run_stage(kind, from_norm ? int(first_off) : -1, from_norm ? xnorm : xin, from_norm ? H : p.xin_cols, e);
+        MK_TRACE(c, p, tb + (k == 1 ? 2 : k == 5 ? 7 : k == 7 ? 9 : 11));
+      } else if (k == 4 || k == 8) {
+        const size_t hn = size_t(p.M) * (p.hq * p.hd / P), an = size_t(p.M) * (p.I / P);
+        const uint64_t* src = k == 4 ? p.head_ll + (blockIdx.x % kMkRep) * hn : p.act_ll + (blockIdx.x % kMkRep) * an;
+        const int nw = k == 4 ? p.hq * p.hd / P : p.I / P;
+        alive = cons_gather<T>(c, p, src, nw, loc_seq(4 * l + (k == 4 ? 2 : 3)), xin, p.xin_cols);
+        MK_TRACE(c, p, tb + (k == 4 ? 6 : 10));
+      } else if (k == 2) {
+        {
+          bool ok = true;
+          for (int li = c.cw; li < n_loc && ok; li += kMkCons) {
+            const int it = blockIdx.x + G * li;
+            T* ks = stg + size_t(li) * stg_elems;
+            const MkItem t = mk_item(p, it, nsp, pos);
+            const bool tr = p.trace && blockIdx.x == 0 && li == 0;
+            const uint32_t sp = uint32_t(l & 1), si = loc_seq(4 * l), so = loc_seq(4 * l + 1);
+            T* vs = ks + stg_elems / 2;
+            switch (p.hd) {
+              case 16: ok = mk_att_item<T, 16>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+              case 32: ok = mk_att_item<T, 32>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+              case 64: ok = mk_att_item<T, 64>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+              default: ok = mk_att_item<T, 128>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
+            }
+            __syncwarp();
           }
-          __syncwarp();
+          if (!ok && lane == 0 && !*abort) mk_fail(c, p);
+          // this warp's staged rows are consumed: fetch the next layer's
+          if (ok && l + 1 < p.L) {
+            __syncwarp();
+            stage_layer(l + 1);
+            staged_layer = l + 1;
+          }
+          MK_TRACE(c, p, tb + 4);
         }
-        if (!ok && lane == 0 && !*abort) mk_fail(c, p);
-        // this warp's staged rows are consumed: fetch the next layer's
-        if (ok && l + 1 < p.L) {
-          __syncwarp();
-          stage_layer(l + 1);
-          staged_layer = l + 1;
-        }
-        MK_TRACE(c, p, tb + 4);
-      }
-      // ---- O: (row, head) pair pr is merged by warp (pr / G) % kMkCons of CTA
-      // pr % G, which publishes the head's output; every CTA then gathers the
-      // merged outputs into xin. The merging warp holds split s (and s + 32)
-      // in lane s: w_s = exp(m_s - max) / sum_s exp(m_s - max) l_s.
+      } else {
       {
-        const int hd = p.hd, hd2 = hd / 2, pairs = p.M * p.hq;
-        const uint32_t seq = loc_seq(4 * l + 1), hseq = loc_seq(4 * l + 2);
-        const size_t head_n = size_t(p.M) * (p.hq * hd / P);
-        bool ok = !*abort;
-        for (int pr = blockIdx.x + G * c.cw; pr < pairs && ok; pr += G * kMkCons) {
-          const uint64_t* part = p.att_ll + size_t(pr) * nsp * (hd + 2);
-          uint4 a[2];
-          a[0] = make_uint4(__float_as_uint(-INFINITY), seq, 0u, seq);
-          a[1] = a[0];
-          {
-            const int na = lane + 32 < nsp ? 2 : lane < nsp ? 1 : 0;
-            auto addr = [&](int b) { return part + size_t(lane + 32 * b) * (hd + 2) + hd; };
-            if (!ll_wait2<2>(p, addr, na, seq, a, abort)) ok = false;
-          }
-          if (!__all_sync(0xffffffffu, ok)) {
-            ok = false;
-            break;
-          }
-          const uint4 a0 = a[0], a1 = a[1];
-          const float m0 = __uint_as_float(a0.x), m1 = __uint_as_float(a1.x);
-          float mx = fmaxf(m0, m1);
+          const int hd = p.hd, hd2 = hd / 2, pairs = p.M * p.hq;
+          const uint32_t seq = loc_seq(4 * l + 1), hseq = loc_seq(4 * l + 2);
+          const size_t head_n = size_t(p.M) * (p.hq * hd / P);
+          bool ok = !*abort;
+          for (int pr = blockIdx.x + G * c.cw; pr < pairs && ok; pr += G * kMkCons) {
+            const uint64_t* part = p.att_ll + size_t(pr) * nsp * (hd + 2);
+            uint4 a[2];
+            a[0] = make_uint4(__float_as_uint(-INFINITY), seq, 0u, seq);
+            a[1] = a[0];
+            {
+              const int na = lane + 32 < nsp ? 2 : lane < nsp ? 1 : 0;
+              auto addr = [&](int b) { return part + size_t(lane + 32 * b) * (hd + 2) + hd; };
+              if (!ll_wait2<2>(p, addr, na, seq, a, abort)) ok = false;
+            }
+            if (!__all_sync(0xffffffffu, ok)) {
+              ok = false;
+              break;
+            }
+            const uint4 a0 = a[0], a1 = a[1];
+            const float m0 = __uint_as_float(a0.x), m1 = __uint_as_float(a1.x);
+            float mx = fmaxf(m0, m1);
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          float w0 = m0 == -INFINITY ? 0.f : expf(m0 - mx), w1 = m1 == -INFINITY ? 0.f : expf(m1 - mx);
-          const float den = warp_sum(fmaf(w0, __uint_as_float(a0.z), w1 * __uint_as_float(a1.z)));
-          const float inv = 1.0f / den;
-          w0 *= inv;
-          w1 *= inv;
-          const int m = pr / p.hq, hh = pr - m * p.hq;
-          // every lane runs every iteration (the shuffles need the whole warp);
-          // lanes past the head's dim pairs load and store nothing
-          for (int dp0 = 0; dp0 < hd2; dp0 += 32) {
-            const int dp = dp0 + lane;
-            const bool act = dp < hd2;
-            float o[2] = {0.f, 0.f};
-            for (int s0 = 0; s0 < nsp; s0 += 4) {
-              uint4 v[4];
-              auto addr = [&](int u) { return part + size_t(s0 + u) * (hd + 2) + 2 * dp; };
-              if (act && ok && !ll_wait2<4>(p, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            float w0 = m0 == -INFINITY ? 0.f : expf(m0 - mx), w1 = m1 == -INFINITY ? 0.f : expf(m1 - mx);
+            const float den = warp_sum(fmaf(w0, __uint_as_float(a0.z), w1 * __uint_as_float(a1.z)));
+            const float inv = 1.0f / den;
+            w0 *= inv;
+            w1 *= inv;
+            const int m = pr / p.hq, hh = pr - m * p.hq;
+            // every lane runs every iteration (the shuffles need the whole warp);
+            // lanes past the head's dim pairs load and store nothing
+            for (int dp0 = 0; dp0 < hd2; dp0 += 32) {
+              const int dp = dp0 + lane;
+              const bool act = dp < hd2;
+              float o[2] = {0.f, 0.f};
+              for (int s0 = 0; s0 < nsp; s0 += 4) {
+                uint4 v[4];
+                auto addr = [&](int u) { return part + size_t(s0 + u) * (hd + 2) + 2 * dp; };
+                if (act && ok && !ll_wait2<4>(p, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int sidx = s0 + u;
-                if (sidx < nsp) {
-                  const float ws = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
-                  if (act) {
-                    o[0] = fmaf(ws, __uint_as_float(v[u].x), o[0]);
-                    o[1] = fmaf(ws, __uint_as_float(v[u].z), o[1]);
+                for (int u = 0; u < 4; ++u) {
+                  const int sidx = s0 + u;
+                  if (sidx < nsp) {
+                    const float ws = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
+                    if (act) {
+                      o[0] = fmaf(ws, __uint_as_float(v[u].x), o[0]);
+                      o[1] = fmaf(ws, __uint_as_float(v[u].z), o[1]);
+                    }
+                  }
+                }
+              }
+              if (act && !*abort) {
+                // dims (2 dp, 2 dp + 1) of head hh: word (hh * hd + 2 dp) / P
+                const size_t w = size_t(m) * (p.hq * hd / P) + (size_t(hh) * hd + 2 * dp) / P;
+#pragma unroll
+                for (int r = 0; r < kMkRep; ++r) {
+                  uint64_t* dst = p.head_ll + r * head_n + w;
+                  if constexpr (P == 2) {
+                    ll_put(dst, LLPack<T>::pack(o), hseq);
+                  } else {
+                    ll_put2(dst, __float_as_uint(o[0]), __float_as_uint(o[1]), hseq);
                   }
                 }
               }
             }
-            if (act && !*abort) {
-              // dims (2 dp, 2 dp + 1) of head hh: word (hh * hd + 2 dp) / P
-              const size_t w = size_t(m) * (p.hq * hd / P) + (size_t(hh) * hd + 2 * dp) / P;
-#pragma unroll
-              for (int r = 0; r < kMkRep; ++r) {
-                uint64_t* dst = p.head_ll + r * head_n + w;
-                if constexpr (P == 2) {
-                  ll_put(dst, LLPack<T>::pack(o), hseq);
-                } else {
-                  ll_put2(dst, __float_as_uint(o[0]), __float_as_uint(o[1]), hseq);
-                }
-              }
-            }
           }
-        }
-        if (!ok && !*abort) mk_fail(c, p);
-        if (cons_sync_or(!ok || *abort)) {
-          alive = false;
-          break;
+          if (!ok && !*abort) mk_fail(c, p);
+          alive = !cons_sync_or(!ok || *abort);
         }
         MK_TRACE(c, p, tb + 5);
-        alive = cons_gather<T>(c, p, p.head_ll + (blockIdx.x % kMkRep) * head_n, p.hq * hd / P, hseq, xin,
-                               p.xin_cols);
-        if (!alive) break;
-        MK_TRACE(c, p, tb + 6);
-        // o_proj -> site 2l+1 of every rank
-        const uint32_t sseq = site_seq(2 * l + 1);
-        run_kind(kMkO, -1, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
-          float r[P];
-#pragma unroll
-          for (int e = 0; e < P; ++e) r[e] = round_t<T>(v[e]);
-          const uint32_t wd = LLPack<T>::pack(r);
-          for (int d = 0; d < cm.world; ++d) ll_put(mk_site(p, d, 2 * l + 1, cm.rank) + size_t(m) * WH + u, wd, sseq);
-        });
       }
-      MK_TRACE(c, p, tb + 7);
-      // ---- GU (its first chunk carries ln2)
-      {
-        const uint32_t off = chunk_wait();
-        const T* gain = reinterpret_cast<const T*>(ring + off);
-        alive = cons_reduce_norm<T>(c, p, 2 * l + 1, site_seq(2 * l + 1), true, gain, xres, xnorm);
-        MK_TRACE(c, p, tb + 8);
-        uint64_t* act = p.act_ll;
-        const size_t act_n = size_t(p.M) * (p.I / P);
-        const uint32_t seq = loc_seq(4 * l + 3);
-        run_kind(kMkGu, int(off), xnorm, H, I2P{}, IP{}, [&](int m, int u, const float* v) {
-          float a[P];
-#pragma unroll
-          for (int e = 0; e < P; ++e) {
-            const float gr = round_t<T>(v[e]), ur = round_t<T>(v[P + e]);
-            a[e] = round_t<T>(gr / (1.0f + expf(-gr))) * ur;
-          }
-          const uint32_t wd = LLPack<T>::pack(a);
-#pragma unroll
-          for (int r = 0; r < kMkRep; ++r) ll_put(act + r * act_n + size_t(m) * (p.I / P) + u, wd, seq);
-        });
-        if (!alive) break;
-      }
-      MK_TRACE(c, p, tb + 9);
-      // ---- DOWN
-      alive = cons_gather<T>(c, p, p.act_ll + (blockIdx.x % kMkRep) * size_t(p.M) * (p.I / P), p.I / P,
-                             loc_seq(4 * l + 3), xin, p.xin_cols);
-      if (!alive) break;
-      MK_TRACE(c, p, tb + 10);
-      {
-        const uint32_t sseq = site_seq(2 * l + 2);
-        run_kind(kMkDown, -1, xin, p.xin_cols, IP{}, IP{}, [&](int m, int u, const float* v) {
-          float r[P];
-#pragma unroll
-          for (int e = 0; e < P; ++e) r[e] = round_t<T>(v[e]);
-          const uint32_t wd = LLPack<T>::pack(r);
-          for (int d = 0; d < cm.world; ++d) ll_put(mk_site(p, d, 2 * l + 2, cm.rank) + size_t(m) * WH + u, wd, sseq);
-        });
-      }
-      MK_TRACE(c, p, tb + 11);
     }
 
     // ---- final norm + LM head + packed argmax (the first LM chunk carries the gain)
@@ -1277,6 +1314,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
     }
   }
   __syncthreads();
+  if (p.trace && blockIdx.x == 0 && threadIdx.x == 32) {
+    p.trace[1101] = clock64();
+    p.trace[1102] = global_ns();
+  }
   // every launch advances the step counter (also one that gave up), so the
   // next launch's sequence numbers match no word written by this one
   if (blockIdx.x == 0 && threadIdx.x == 0) p.comm.ctl()[kCtlStep] = step;

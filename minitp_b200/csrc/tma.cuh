@@ -85,6 +85,12 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no shared memory involved).
+// src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Named barrier over `nthreads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -156,5 +156,8 @@ def test_synthetic_protocol_matches_fixture_prompt():
 def test_launch_count_formula():
     from bench import launches_per_generation
 
-    # prefill: embed + 5 per layer + consume passes (2 per layer + final) + LM head
-    assert launches_per_generation(2, 2, 8) == (1 + 10 + 5 + 1) + 2 + 1 + (1 + 10 + 2)
+    # prefill: embed + 5 per layer + consume passes (2 per layer + final) + LM head;
+    # then argmax (2), the position seed (1) and the decode steps
+    assert launches_per_generation(2, 2, 8, 1 + 10 + 2) == (1 + 10 + 5 + 1) + 2 + 1 + (1 + 10 + 2)
+    # one decode megakernel launch per step
+    assert launches_per_generation(2, 5, 8, 1) == (1 + 10 + 5 + 1) + 2 + 1 + 4
