@@ -153,6 +153,17 @@ def kv_bytes_per_token(model, batch: int, avg_len: float) -> float:
     return per_pos * avg_len * batch * len(model.model.layers)
 
 
+# DRAM bytes (read + write) of one decode_mk_kernel launch from an ncu capture
+# (profiles/decode_mk_kernel_qwen05b_tp1_b1.md), keyed by (model, batch, TP).
+MK_TRAFFIC = {("qwen2.5-0.5b", 1, 1): 994_280_704}
+
+
+def measured_traffic(args, world: int, step_launches: int):
+    if step_launches != 1:
+        return None
+    return MK_TRAFFIC.get((args.model, args.batch, world))
+
+
 def launches_per_generation(n_layers: int, new_tokens: int, prefill_tokens: int, step_launches: int) -> int:
     """minitp_b200 kernel launches of one fixed-length generation.
 
@@ -366,7 +377,8 @@ def run_b200(args, cfg, prompt_len, new_tokens):
             "roofline": {"bound": "hbm",
                          "kernel": "decode_mk_kernel" if step_launches == 1 else "decode kernel chain",
                          "achieved": round(tok_gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(tok_gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "frac": round(tok_gbs / peak, 4), "traffic": measured_traffic(args, world, step_launches),
+                         "peak_kind": peak_kind,
                          "bytes_per_launch": round(wb + kvb), "weight_bytes": wb, "kv_bytes": round(kvb),
                          "us_per_launch": round(ms_per_token * 1e3, 3),
                          "timing": "CUDA events over the graph replays of the decode step (one launch each)"},

@@ -281,14 +281,22 @@ int embed_run(int dtype, const EmbedParams& p, int grid, cudaStream_t st) {
 int ar_norm_run(int dtype, ArNormParams p, cudaStream_t st) {
   if (size_t(p.rows) * p.H * dsize(dtype) > p.comm.slot_bytes && p.comm.world > 1)
     return fail(MTPB_ERR_INVALID, "allreduce: message larger than the communicator slot");
+  // LL words (8 bytes per 2 bf16 / 1 fp32 value) when they fit the slot
+  const int P = dtype == MTPB_BF16 ? 2 : 1;
+  const bool ll = p.comm.world > 1 && p.H % P == 0 && size_t(p.rows) * (p.H / P) * 8 <= p.comm.slot_bytes;
   // rows per CTA: spread rows over the SMs, at most kMaxCtas CTAs
   const int sms = sm_count();
   int ctas = std::min(p.rows, std::min(sms * 2, kMaxCtas));
   ctas = std::max(ctas, 1);
   p.rpc = (p.rows + ctas - 1) / ctas;
   ctas = (p.rows + p.rpc - 1) / p.rpc;
-  if (dtype == MTPB_BF16) return launch(ar_norm_kernel<bf16>, dim3(ctas), dim3(256), 0, st, p);
-  if (dtype == MTPB_F32) return launch(ar_norm_kernel<float>, dim3(ctas), dim3(256), 0, st, p);
+  if (ll) p.chan = 3;  // LL words never share a slot with raw data
+  if (dtype == MTPB_BF16)
+    return ll ? launch(ar_norm_ll_kernel<bf16>, dim3(ctas), dim3(256), 0, st, p)
+              : launch(ar_norm_kernel<bf16>, dim3(ctas), dim3(256), 0, st, p);
+  if (dtype == MTPB_F32)
+    return ll ? launch(ar_norm_ll_kernel<float>, dim3(ctas), dim3(256), 0, st, p)
+              : launch(ar_norm_kernel<float>, dim3(ctas), dim3(256), 0, st, p);
   return fail(MTPB_ERR_INVALID, "unsupported dtype");
 }
 

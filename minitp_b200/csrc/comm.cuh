@@ -20,14 +20,15 @@
 // carries standalone collectives (all_reduce, the fused AR+RMSNorm op), whose
 // sequence numbers come from a device call counter. Channel 2 belongs to the
 // decode megakernel, whose data words carry their own sequence numbers
-// (LL words) and need no flags.
+// (LL words) and need no flags; channel 3 carries the LL form of the
+// standalone collectives (same counter as channel 1).
 #pragma once
 
 #include "common.cuh"
 
 namespace mtpb {
 
-constexpr int kChannels = 3;
+constexpr int kChannels = 4;
 constexpr int kMaxCtas = 1024;
 constexpr size_t kCtlBytes = 4096;
 constexpr size_t kFlagBytes = size_t(kChannels) * 2 * kMaxRanks * kMaxCtas * sizeof(uint32_t);

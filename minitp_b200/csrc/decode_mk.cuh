@@ -41,6 +41,7 @@
 #include <type_traits>
 
 #include "comm.cuh"
+#include "ll.cuh"
 #include "tma.cuh"
 
 namespace mtpb {
@@ -61,83 +62,6 @@ constexpr int kMkRep = 4;
 
 // GEMV stage kinds
 enum : int { kMkQkv = 0, kMkO = 1, kMkGu = 2, kMkDown = 3, kMkLm = 4, kMkKinds = 5 };
-
-// ---------------------------------------------------------------------------
-// LL words
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void ll_put(uint64_t* dst, uint32_t payload, uint32_t seq) {
-  const uint64_t w = (uint64_t(seq) << 32) | payload;
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
-}
-// two words {a, seq}, {b, seq} in one 16-byte store (two 64-bit elements,
-// each of which validates itself)
-__device__ __forceinline__ void ll_put2(uint64_t* dst, uint32_t a, uint32_t b, uint32_t seq) {
-  const uint64_t w0 = (uint64_t(seq) << 32) | a, w1 = (uint64_t(seq) << 32) | b;
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(w0), "l"(w1) : "memory");
-}
-__device__ __forceinline__ uint2 ll_ld(const uint64_t* src) {
-  uint64_t w;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
-  return make_uint2(uint32_t(w), uint32_t(w >> 32));
-}
-// {payload0, seq0, payload1, seq1}
-__device__ __forceinline__ uint4 ll_ld2(const uint64_t* src) {
-  uint64_t a, b;
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
-  return make_uint4(uint32_t(a), uint32_t(a >> 32), uint32_t(b), uint32_t(b >> 32));
-}
-__device__ __forceinline__ bool ll_ok2(const uint4& v, uint32_t seq) { return v.y == seq && v.w == seq; }
-
-// Re-poll one word / one 16-byte pair until it carries seq (the slow path,
-// kept out of line; results come back by value so the callers' arrays stay in
-// registers). ok == 0 when the CTA's abort flag is raised or `budget_ns`
-// passed.
-struct LLSpin {
-  uint4 v;
-  uint32_t ok;
-};
-__device__ __noinline__ LLSpin ll_spin_any(const uint64_t* src, uint32_t seq, int wide, uint64_t budget_ns,
-                                           volatile int* abort, uint32_t backoff_ns) {
-  LLSpin r;
-  const uint64_t t0 = global_ns();
-  for (uint32_t n = 1;; ++n) {
-    if (backoff_ns) __nanosleep(backoff_ns);
-    if (wide) {
-      r.v = ll_ld2(src);
-      if (ll_ok2(r.v, seq)) break;
-    } else {
-      const uint2 a = ll_ld(src);
-      r.v = make_uint4(a.x, a.y, 0u, 0u);
-      if (a.y == seq) break;
-    }
-    if ((n & 15) == 0 && (*abort || global_ns() - t0 > budget_ns)) {
-      r.ok = 0;
-      return r;
-    }
-  }
-  r.ok = 1;
-  return r;
-}
-
-// T values per LL word and their packing (bf16: two values, low half first)
-template <typename T> struct LLPack;
-template <> struct LLPack<float> {
-  static constexpr int kPer = 1;
-  __device__ static uint32_t pack(const float* v) { return __float_as_uint(v[0]); }
-  __device__ static void unpack(uint32_t w, float* v) { v[0] = __uint_as_float(w); }
-};
-template <> struct LLPack<bf16> {
-  static constexpr int kPer = 2;
-  __device__ static uint32_t pack(const float* v) {
-    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(v[0]));
-    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(v[1]));
-    return lo | (hi << 16);
-  }
-  __device__ static void unpack(uint32_t w, float* v) {
-    v[0] = __uint_as_float(w << 16);
-    v[1] = __uint_as_float(w & 0xFFFF0000u);
-  }
-};
 
 // shared-memory loads by 32-bit shared address
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
@@ -247,59 +171,6 @@ __device__ __forceinline__ bool ll_spin2(const MkParams& p, const uint64_t* src,
   const LLSpin r = ll_spin_any(src, seq, 1, p.budget_ns, abort, p.spin_ns);
   v = r.v;
   return r.ok != 0;
-}
-
-// Poll up to NB 16-byte LL pairs (or 8-byte words) until all carry seq.
-// Every round issues the loads of all that are still missing, so a round
-// costs one memory round trip however many are late. False on timeout or
-// abort.
-template <int NB, typename Addr>
-__device__ __forceinline__ bool ll_wait2(const MkParams& p, Addr addr, int n, uint32_t seq, uint4 (&v)[NB],
-                                         volatile int* abort) {
-  uint32_t pend = 0;
-#pragma unroll
-  for (int b = 0; b < NB; ++b)
-    if (b < n) v[b] = ll_ld2(addr(b));
-#pragma unroll
-  for (int b = 0; b < NB; ++b)
-    if (b < n && !ll_ok2(v[b], seq)) pend |= 1u << b;
-  if (!pend) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (p.spin_ns) __nanosleep(p.spin_ns);
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if (pend & (1u << b)) v[b] = ll_ld2(addr(b));
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if ((pend & (1u << b)) && ll_ok2(v[b], seq)) pend &= ~(1u << b);
-    if (!pend) return true;
-    if ((it & 15) == 0 && (*abort || global_ns() - t0 > p.budget_ns)) return false;
-  }
-}
-template <int NB, typename Addr>
-__device__ __forceinline__ bool ll_wait1(const MkParams& p, Addr addr, int n, uint32_t seq, uint2 (&v)[NB],
-                                         volatile int* abort) {
-  uint32_t pend = 0;
-#pragma unroll
-  for (int b = 0; b < NB; ++b)
-    if (b < n) v[b] = ll_ld(addr(b));
-#pragma unroll
-  for (int b = 0; b < NB; ++b)
-    if (b < n && v[b].y != seq) pend |= 1u << b;
-  if (!pend) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (p.spin_ns) __nanosleep(p.spin_ns);
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if (pend & (1u << b)) v[b] = ll_ld(addr(b));
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if ((pend & (1u << b)) && v[b].y == seq) pend &= ~(1u << b);
-    if (!pend) return true;
-    if ((it & 15) == 0 && (*abort || global_ns() - t0 > p.budget_ns)) return false;
-  }
 }
 
 #define MK_TRACE(c, p, idx)                                                                   \
@@ -421,7 +292,7 @@ __device__ __forceinline__ bool cons_reduce_norm(const MkCtx& c, const MkParams&
       for (int r0 = 0; r0 < cm.world; r0 += 4) {
         uint4 v[4];
         auto addr = [&](int r) { return mk_site(p, cm.rank, site, r0 + r) + size_t(m) * W + 2 * i; };
-        if (!ll_wait2<4>(p, addr, min(4, cm.world - r0), seq, v, c.abort)) ok = false;
+        if (!ll_wait2<4>(p.budget_ns, p.spin_ns, addr, min(4, cm.world - r0), seq, v, c.abort)) ok = false;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           if (r0 + r < cm.world) {
@@ -468,7 +339,7 @@ __device__ __forceinline__ bool cons_gather(const MkCtx& c, const MkParams& p, c
       const int i = b0 + b * kMkConsThreads, m = i / nl, w = i - m * nl;
       return src + size_t(m) * n + 2 * w;
     };
-    if (!ll_wait2<NB>(p, addr, nb, seq, v, c.abort)) ok = false;
+    if (!ll_wait2<NB>(p.budget_ns, p.spin_ns, addr, nb, seq, v, c.abort)) ok = false;
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const int i = b0 + b * kMkConsThreads;
@@ -715,7 +586,7 @@ __device__ __forceinline__ bool mk_att_item(const MkCtx& c, const MkParams& p, c
     uint2 v[3];
     const uint64_t* src[3] = {qw + w, kw + w, vw + w};
     auto addr = [&](int b) { return src[b]; };
-    if (!ll_wait1<3>(p, addr, has_new ? 3 : 1, seq_in, v, c.abort)) ok = false;
+    if (!ll_wait1<3>(p.budget_ns, p.spin_ns, addr, has_new ? 3 : 1, seq_in, v, c.abort)) ok = false;
     LLPack<T>::unpack(v[0].x, q + w * P);
     if (has_new) {
       LLPack<T>::unpack(v[1].x, kn + w * P);
@@ -1158,7 +1029,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
             {
               const int na = lane + 32 < nsp ? 2 : lane < nsp ? 1 : 0;
               auto addr = [&](int b) { return part + size_t(lane + 32 * b) * (hd + 2) + hd; };
-              if (!ll_wait2<2>(p, addr, na, seq, a, abort)) ok = false;
+              if (!ll_wait2<2>(p.budget_ns, p.spin_ns, addr, na, seq, a, abort)) ok = false;
             }
             if (!__all_sync(0xffffffffu, ok)) {
               ok = false;
@@ -1184,7 +1055,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
               for (int s0 = 0; s0 < nsp; s0 += 4) {
                 uint4 v[4];
                 auto addr = [&](int u) { return part + size_t(s0 + u) * (hd + 2) + 2 * dp; };
-                if (act && ok && !ll_wait2<4>(p, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
+                if (act && ok && !ll_wait2<4>(p.budget_ns, p.spin_ns, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                   const int sidx = s0 + u;

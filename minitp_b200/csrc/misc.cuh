@@ -3,6 +3,7 @@
 #pragma once
 
 #include "comm.cuh"
+#include "ll.cuh"
 
 namespace mtpb {
 
@@ -274,6 +275,88 @@ __global__ void __launch_bounds__(256) ar_norm_kernel(const ArNormParams p) {
       for (int j = threadIdx.x; j < p.H; j += blockDim.x) {
         const size_t off = size_t(row) * p.H + j;
         const float x = to_f(static_cast<const T*>(p.out_res)[off]);
+        static_cast<T*>(p.out_norm)[off] = from_f<T>(__fmul_rn(__fmul_rn(x, rinv), to_f(gain[j])));
+      }
+    }
+  }
+  advance_counter(c, kCtlColl, kCtlCollDone, seq);
+}
+
+// The same operation over LL words, for messages whose LL form (8 bytes per
+// kPer values) fits the communicator slot: every rank pushes its partial rows
+// as LL words into channel `chan` of every rank (parity seq & 1), then each
+// CTA reads its rows' words of every rank (all ranks' loads in flight
+// together), sums them in rank order and finishes its rows. No fence and no
+// flag: the words carry the call's sequence number.
+template <typename T>
+__global__ void __launch_bounds__(256) ar_norm_ll_kernel(const ArNormParams p) {
+  constexpr int P = LLPack<T>::kPer;
+  __shared__ float red[32];
+  __shared__ int abort_s;
+  pdl_launch();
+  pdl_wait();
+  const Comm& c = p.comm;
+  const uint32_t seq = ld_volatile_u32(c.ctl() + kCtlColl) + 1u;
+  const int par = seq & 1;
+  const int W = p.H / P;
+  const int r0 = blockIdx.x * p.rpc, r1 = min(p.rows, r0 + p.rpc);
+  if (threadIdx.x == 0) abort_s = 0;
+  __syncthreads();
+  const T* src = static_cast<const T*>(p.partial);
+  for (int i = threadIdx.x; i < (r1 - r0) * W; i += blockDim.x) {
+    const size_t wi = size_t(r0) * W + i;
+    float f[P];
+#pragma unroll
+    for (int e = 0; e < P; ++e) f[e] = to_f(src[wi * P + e]);
+    const uint32_t u = LLPack<T>::pack(f);
+    for (int d = 0; d < c.world; ++d) ll_put(reinterpret_cast<uint64_t*>(c.data(d, p.chan, par, c.rank)) + wi, u, seq);
+  }
+  const T* gain = static_cast<const T*>(p.gain);
+  const T* bias = static_cast<const T*>(p.bias);
+  const T* resid = static_cast<const T*>(p.residual);
+  T* out_res = static_cast<T*>(p.out_res);
+  bool ok = true;
+  for (int row = r0; row < r1; ++row) {
+    float ss = 0.f;
+    for (int w = threadIdx.x; w < W; w += blockDim.x) {
+      const size_t wi = size_t(row) * W + w;
+      uint2 v[kMaxRanks];
+      auto addr = [&](int r) { return reinterpret_cast<const uint64_t*>(c.data(c.rank, p.chan, par, r)) + wi; };
+      if (ok && !ll_wait1<kMaxRanks>(c.timeout_ns, 0u, addr, c.world, seq, v, &abort_s)) {
+        ok = false;
+        abort_s = 1;
+        atomicOr(c.status(), kStatusTimeout);
+      }
+      float s[P];
+#pragma unroll
+      for (int e = 0; e < P; ++e) s[e] = 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        if (r < c.world) {
+          float f[P];
+          LLPack<T>::unpack(v[r].x, f);
+#pragma unroll
+          for (int e = 0; e < P; ++e) s[e] += f[e];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < P; ++e) {
+        const int j = w * P + e;
+        const size_t off = size_t(row) * p.H + j;
+        float o = round_t<T>(s[e]);
+        if (bias) o = round_t<T>(o + to_f(bias[j]));
+        const float x = resid ? round_t<T>(to_f(resid[off]) + o) : o;
+        out_res[off] = from_f<T>(x);
+        ss += x * x;
+      }
+    }
+    if (p.out_norm) {
+      const float tot = block_sum(ss, red);
+      const float rinv = rsqrtf(tot / float(p.H) + p.eps);
+      __syncthreads();
+      for (int j = threadIdx.x; j < p.H; j += blockDim.x) {
+        const size_t off = size_t(row) * p.H + j;
+        const float x = to_f(out_res[off]);
         static_cast<T*>(p.out_norm)[off] = from_f<T>(__fmul_rn(__fmul_rn(x, rinv), to_f(gain[j])));
       }
     }
