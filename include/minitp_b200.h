@@ -46,6 +46,9 @@ int mtpb_set_prefetch_cap(uint32_t bytes);
 /* GEMV grid size in CTAs per SM (default 2, range [1, 8]); applies to later launches
  * and to graph captures made after the call. */
 int mtpb_set_gemv_ctas_per_sm(int n);
+/* bf16 projections with at least `rows` rows (default 64) run on the tensor-core
+ * (tcgen05) GEMM instead of the GEMV kernel; a large value keeps them on the GEMV. */
+int mtpb_set_tc_min_rows(int rows);
 
 /* ------------------------------------------------------- communicator
  * Peer-memory communicator over NVLink (one per rank; TP group == world).

@@ -16,6 +16,9 @@
 #include "minitp_b200.h"
 #include "misc.cuh"
 #include "decode_mk.cuh"
+#include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
 
 using namespace mtpb;
 
@@ -143,8 +146,95 @@ int gemv_launch(GemvParams p, cudaStream_t st) {
   }
 }
 
+// ------------------------------------------------------------------ tensor-core GEMM (prefill)
+bool capturing(cudaStream_t st);
+int g_tc_min_rows = 64;  // bf16 projections of at least this many rows use tcgen05
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over rows x cols (row stride ld elements), box
+// box_rows x 64 columns, 128-byte swizzle; out-of-range boxes read zeros.
+int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(MTPB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {uint32_t(kTcBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTPB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return MTPB_OK;
+}
+
+template <int EPI>
+bool tc_eligible(int dtype, const GemvParams& p) {
+  if (dtype != MTPB_BF16 || p.M < g_tc_min_rows || p.x_mode != 0 || !p.x) return false;
+  if (EPI != kEpiStore && EPI != kEpiSwiglu && EPI != kEpiRope && EPI != kEpiPush) return false;
+  if (p.K % 8 || p.ldx % 8 || p.K < kTcBK || !aligned16(p.x) || !aligned16(p.w)) return false;
+  if (EPI == kEpiRope && (p.hd < 32 || p.hd > 128 || kTcBN % p.hd)) return false;
+  if (EPI == kEpiSwiglu && (p.N % 2)) return false;
+  return true;
+}
+
+template <int EPI>
+int tc_tiles_n(const GemvParams& p) {
+  if (EPI == kEpiSwiglu) return ((p.N >> 1) + kTcBN / 2 - 1) / (kTcBN / 2);
+  return (p.N + kTcBN - 1) / kTcBN;
+}
+
+template <int EPI>
+int tc_grid(const GemvParams& p) {
+  return tc_tiles_n<EPI>(p) * ((p.M + kTcBM - 1) / kTcBM);
+}
+
+template <int EPI>
+int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
+  TcParams tp;
+  tp.g = g;
+  tp.tiles_n = tc_tiles_n<EPI>(g);
+  tp.budget_ns = 2000000000ull;
+  if (EPI == kEpiPush && tc_grid<EPI>(g) > kMaxCtas)
+    return fail(MTPB_ERR_INVALID, "tensor-core GEMM: too many producer tiles for one collective");
+  CUtensorMap mx, mw;
+  MTPB_TRY(make_map_bf16(&mx, g.x, uint64_t(g.M), uint64_t(g.K), uint64_t(g.ldx), kTcBM));
+  MTPB_TRY(make_map_bf16(&mw, g.w, uint64_t(g.N), uint64_t(g.K), uint64_t(g.K), EPI == kEpiSwiglu ? kTcBN / 2 : kTcBN));
+  auto kern = gemm_tc_kernel<bf16, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (capturing(st)) return fail(MTPB_ERR_INVALID, "tensor-core GEMM: run one call eagerly before graph capture");
+    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem)));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tc_grid<EPI>(g));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  MTPB_CUDA(cudaLaunchKernelEx(&cfg, kern, tp, mx, mw));
+  return MTPB_OK;
+}
+
 template <int EPI>
 int gemv_dispatch(int dtype, const GemvParams& p, cudaStream_t st) {
+  if (tc_eligible<EPI>(dtype, p)) return gemm_tc_launch<EPI>(p, st);
   if (dtype == MTPB_BF16) return gemv_launch<bf16, EPI>(p, st);
   if (dtype == MTPB_F32) return gemv_launch<float, EPI>(p, st);
   return fail(MTPB_ERR_INVALID, "unsupported dtype");
@@ -153,6 +243,11 @@ int gemv_dispatch(int dtype, const GemvParams& p, cudaStream_t st) {
 // grid size a GEMV launch will use (producer CTA count of a push site)
 int gemv_grid(int units) {
   return std::max(1, std::min(units, std::min(sm_count() * g_gemv_ctas_per_sm, kMaxCtas)));
+}
+
+// producer CTA count of a push-epilogue dispatch (GEMV or tensor-core GEMM)
+int push_grid(int dtype, const GemvParams& p) {
+  return tc_eligible<kEpiPush>(dtype, p) ? tc_grid<kEpiPush>(p) : gemv_grid(p.units);
 }
 
 GemvParams gemv_base(const void* w, const void* bias, int M, int N, int K, int units) {
@@ -486,7 +581,6 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
   int nprod = egrid;
   int cur = 0;  // residual ping-pong index holding the current residual
   bool has_res = false;
-  const int grid_o = gemv_grid(H), grid_down = gemv_grid(H);
 
   auto consume_into = [&](GemvParams& g, uint32_t site, const void* gain) {
     g.comm = comm;
@@ -559,7 +653,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
       g.out_seq = SeqRef{uint32_t(2 * l + 1), nsite, 0u};
       g.out_chan = chan;
       MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
-      nprod = grid_o;
+      nprod = push_grid(d.dtype, g);
     }
     // gate/up + SwiGLU, consuming site 2l+1
     {
@@ -578,7 +672,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
       g.out_seq = SeqRef{uint32_t(2 * l + 2), nsite, 0u};
       g.out_chan = chan;
       MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
-      nprod = grid_down;
+      nprod = push_grid(d.dtype, g);
     }
   }
 
@@ -1245,6 +1339,12 @@ int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
   g_mk_lm_kb = lm_chunk_kb;
   g_mk_l2hint = l2_flags & 1;
   g_mk_l2ahead = (l2_flags >> 1) & 1;
+  return MTPB_OK;
+}
+
+int mtpb_set_tc_min_rows(int rows) {
+  if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
+  g_tc_min_rows = rows;
   return MTPB_OK;
 }
 

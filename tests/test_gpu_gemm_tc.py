@@ -1,0 +1,86 @@
+"""Tensor-core (tcgen05) GEMM of the bf16 prefill projections.
+
+bf16 projections with at least 64 rows run on the tensor-core kernel
+(gemm_tc.cuh); these tests pin its output against a float64 reference of the
+same bf16 inputs, with the store, SwiGLU and fused QKV + RoPE + KV-append
+epilogues, full and partial tiles, and K that is not a multiple of the
+64-element K block.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_linear(x, w, b=None):
+    y = x.double() @ w.double().t()
+    return y if b is None else y + b.double()
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 128, 64), (128, 1152, 896), (200, 300, 896), (128, 896, 4864),
+                                   (256, 640, 1000), (130, 4096, 896)])
+def test_tc_linear(lib, M, N, K):
+    from minitp_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16)
+    y = ops.linear(x.cuda(), w.cuda(), b.cuda()).cpu()
+    ref = _ref_linear(x, w, b)
+    # fp32 accumulation in tensor memory, one rounding to bf16
+    torch.testing.assert_close(y.double(), ref.to(torch.bfloat16).double(), atol=1e-3, rtol=2 ** -7)
+    # the GEMV kernel on the same inputs agrees to the same tolerance
+    lib.mtpb_set_tc_min_rows(1 << 30)
+    try:
+        y2 = ops.linear(x.cuda(), w.cuda(), b.cuda()).cpu()
+    finally:
+        lib.mtpb_set_tc_min_rows(64)
+    torch.testing.assert_close(y.float(), y2.float(), atol=1e-3, rtol=2 ** -7)
+
+
+@pytest.mark.parametrize("M,I,K", [(128, 2432, 896), (96, 200, 256)])
+def test_tc_swiglu(lib, M, I, K):
+    from minitp_b200 import ops
+
+    g = torch.Generator().manual_seed(M + I + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, generator=g) * 0.02).to(torch.bfloat16)
+    y = ops.linear_swiglu(x.cuda(), w.cuda()).cpu()
+    gate, up = torch.chunk(_ref_linear(x, w).to(torch.bfloat16), 2, dim=-1)
+    ref = F.silu(gate.float()).to(torch.bfloat16).float() * up.float()
+    torch.testing.assert_close(y.float(), ref.to(torch.bfloat16).float(), atol=1e-3, rtol=2 ** -6)
+
+
+@pytest.mark.parametrize("hq,hkv,hd,T", [(14, 2, 64, 128), (7, 1, 64, 100), (7, 1, 128, 64)])
+def test_tc_qkv_rope(lib, hq, hkv, hd, T):
+    """Prefill QKV projection + bias + RoPE + KV append through the tensor-core path."""
+    from minitp_b200 import ops
+    from minitp_b200.rope import rope_tables
+
+    torch.manual_seed(hq * 10 + hd + T)
+    B, H, cap = 1, 896, 512
+    x = torch.randn(B, T, H).to(torch.bfloat16)
+    w = (torch.randn((hq + 2 * hkv) * hd, H) * 0.05).to(torch.bfloat16)
+    b = (torch.randn((hq + 2 * hkv) * hd) * 0.05).to(torch.bfloat16)
+    kc = torch.zeros(B, hkv, cap, hd).to(torch.bfloat16)
+    vc = torch.zeros(B, hkv, cap, hd).to(torch.bfloat16)
+    cos, sin = rope_tables(hd, 1e6, 4096)
+    kcg, vcg = kc.cuda(), vc.cuda()
+    q = ops.qkv_rope(x.cuda(), w.cuda(), b.cuda(), kcg, vcg, hq, hkv, 0, None, cos.cuda(), sin.cuda()).cpu()
+    y = (x.double() @ w.double().t() + b.double()).to(torch.bfloat16)
+    qo, ko, vo = torch.split(y, [hq * hd, hkv * hd, hkv * hd], dim=-1)
+    qo = qo.reshape(B, T, hq, hd).transpose(1, 2)
+    ko = ko.reshape(B, T, hkv, hd).transpose(1, 2)
+    vo = vo.reshape(B, T, hkv, hd).transpose(1, 2)
+    pos = torch.arange(T)
+    qo, ko = om.apply_rope(qo, cos[pos], sin[pos]), om.apply_rope(ko, cos[pos], sin[pos])
+    tol = dict(atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(q.reshape(B, T, hq, hd).transpose(1, 2).float(), qo.float(), **tol)
+    torch.testing.assert_close(kcg.cpu()[:, :, :T].float(), ko.float(), **tol)
+    torch.testing.assert_close(vcg.cpu()[:, :, :T].float(), vo.float(), **tol)
+    assert torch.equal(kcg.cpu()[:, :, T:], kc[:, :, T:])
