@@ -165,7 +165,26 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 2-D bf16 tensor map over rows x cols (row stride ld elements), box
 // box_rows x 64 columns, 128-byte swizzle; out-of-range boxes read zeros.
+// Encoded maps are kept in a small cache keyed on all of those fields (a map
+// holds nothing else), so a prefill chain re-encodes only new buffers.
 int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  struct Entry {
+    const void* ptr;
+    uint64_t rows, cols, ld;
+    uint32_t box;
+    CUtensorMap map;
+  };
+  static Entry cache[64];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i) {
+    const Entry& e = cache[i];
+    if (e.ptr == ptr && e.rows == rows && e.cols == cols && e.ld == ld && e.box == box_rows) {
+      *map = e.map;
+      return MTPB_OK;
+    }
+  }
   auto enc = tensor_map_encoder();
   if (!enc) return fail(MTPB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[2] = {cols, rows};
@@ -176,6 +195,10 @@ int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t col
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MTPB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  Entry& e = cache[next];
+  e = Entry{ptr, rows, cols, ld, box_rows, *map};
+  next = (next + 1) % 64;
+  used = std::max(used, next == 0 ? 64 : next);
   return MTPB_OK;
 }
 
@@ -184,44 +207,54 @@ bool tc_eligible(int dtype, const GemvParams& p) {
   if (dtype != MTPB_BF16 || p.M < g_tc_min_rows || p.x_mode != 0 || !p.x) return false;
   if (EPI != kEpiStore && EPI != kEpiSwiglu && EPI != kEpiRope && EPI != kEpiPush) return false;
   if (p.K % 8 || p.ldx % 8 || p.K < kTcBK || !aligned16(p.x) || !aligned16(p.w)) return false;
-  if (EPI == kEpiRope && (p.hd < 32 || p.hd > 128 || kTcBN % p.hd)) return false;
+  if (EPI == kEpiRope && (p.hd < 32 || p.hd > 128 || 128 % p.hd)) return false;
   if (EPI == kEpiSwiglu && (p.N % 2)) return false;
   return true;
 }
 
+// output tiles along N for a tile width of BN accumulator columns
 template <int EPI>
-int tc_tiles_n(const GemvParams& p) {
-  if (EPI == kEpiSwiglu) return ((p.N >> 1) + kTcBN / 2 - 1) / (kTcBN / 2);
-  return (p.N + kTcBN - 1) / kTcBN;
+int tc_tiles_n(const GemvParams& p, int bn) {
+  if (EPI == kEpiSwiglu) return ((p.N >> 1) + bn / 2 - 1) / (bn / 2);
+  return (p.N + bn - 1) / bn;
 }
 
+// 256-column tiles when they alone give every SM a tile, else 128 (more CTAs
+// on the small-M, HBM-bound shapes)
+template <int EPI>
+int tc_bn(const GemvParams& p) {
+  const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
+  return tiles_m * tc_tiles_n<EPI>(p, 256) >= sm_count() ? 256 : 128;
+}
+
+// persistent grid: one CTA per SM at most
 template <int EPI>
 int tc_grid(const GemvParams& p) {
-  return tc_tiles_n<EPI>(p) * ((p.M + kTcBM - 1) / kTcBM);
+  const int tiles = tc_tiles_n<EPI>(p, tc_bn<EPI>(p)) * ((p.M + kTcBM - 1) / kTcBM);
+  return std::min(tiles, sm_count());
 }
 
-template <int EPI>
-int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
+template <int EPI, int BN>
+int gemm_tc_launch_bn(const GemvParams& g, cudaStream_t st) {
   TcParams tp;
   tp.g = g;
-  tp.tiles_n = tc_tiles_n<EPI>(g);
+  tp.tiles_m = (g.M + kTcBM - 1) / kTcBM;
+  tp.tiles_n = tc_tiles_n<EPI>(g, BN);
   tp.budget_ns = 2000000000ull;
-  if (EPI == kEpiPush && tc_grid<EPI>(g) > kMaxCtas)
-    return fail(MTPB_ERR_INVALID, "tensor-core GEMM: too many producer tiles for one collective");
   CUtensorMap mx, mw;
   MTPB_TRY(make_map_bf16(&mx, g.x, uint64_t(g.M), uint64_t(g.K), uint64_t(g.ldx), kTcBM));
-  MTPB_TRY(make_map_bf16(&mw, g.w, uint64_t(g.N), uint64_t(g.K), uint64_t(g.K), EPI == kEpiSwiglu ? kTcBN / 2 : kTcBN));
-  auto kern = gemm_tc_kernel<bf16, EPI>;
+  MTPB_TRY(make_map_bf16(&mw, g.w, uint64_t(g.N), uint64_t(g.K), uint64_t(g.K), EPI == kEpiSwiglu ? BN / 2 : BN));
+  auto kern = gemm_tc_kernel<bf16, EPI, BN>;
   static bool attr_set = false;
   if (!attr_set) {
     if (capturing(st)) return fail(MTPB_ERR_INVALID, "tensor-core GEMM: run one call eagerly before graph capture");
-    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem)));
+    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::kSmem)));
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tc_grid<EPI>(g));
+  cfg.gridDim = dim3(std::min(tp.tiles_m * tp.tiles_n, sm_count()));
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -230,6 +263,11 @@ int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
   cfg.numAttrs = g_pdl ? 1 : 0;
   MTPB_CUDA(cudaLaunchKernelEx(&cfg, kern, tp, mx, mw));
   return MTPB_OK;
+}
+
+template <int EPI>
+int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
+  return tc_bn<EPI>(g) == 256 ? gemm_tc_launch_bn<EPI, 256>(g, st) : gemm_tc_launch_bn<EPI, 128>(g, st);
 }
 
 template <int EPI>

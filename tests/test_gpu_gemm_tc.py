@@ -3,8 +3,9 @@
 bf16 projections with at least 64 rows run on the tensor-core kernel
 (gemm_tc.cuh); these tests pin its output against a float64 reference of the
 same bf16 inputs, with the store, SwiGLU and fused QKV + RoPE + KV-append
-epilogues, full and partial tiles, and K that is not a multiple of the
-64-element K block.
+epilogues, full and partial tiles, K that is not a multiple of the 64-element
+K block, both tile widths (128 and 256 accumulator columns) and persistent
+CTAs that take several tiles each (both tensor-memory accumulators in turn).
 """
 
 import pytest
@@ -22,7 +23,8 @@ def _ref_linear(x, w, b=None):
 
 
 @pytest.mark.parametrize("M,N,K", [(64, 128, 64), (128, 1152, 896), (200, 300, 896), (128, 896, 4864),
-                                   (256, 640, 1000), (130, 4096, 896)])
+                                   (256, 640, 1000), (130, 4096, 896),
+                                   (2048, 9728, 896), (1152, 2304, 512), (300, 20000, 128)])
 def test_tc_linear(lib, M, N, K):
     from minitp_b200 import ops
 
@@ -43,7 +45,8 @@ def test_tc_linear(lib, M, N, K):
     torch.testing.assert_close(y.float(), y2.float(), atol=1e-3, rtol=2 ** -7)
 
 
-@pytest.mark.parametrize("M,I,K", [(128, 2432, 896), (96, 200, 256)])
+@pytest.mark.parametrize("M,I,K", [(128, 2432, 896), (96, 200, 256), (1024, 4864, 896),
+                                   (1000, 2500, 192)])
 def test_tc_swiglu(lib, M, I, K):
     from minitp_b200 import ops
 
@@ -56,14 +59,15 @@ def test_tc_swiglu(lib, M, I, K):
     torch.testing.assert_close(y.float(), ref.to(torch.bfloat16).float(), atol=1e-3, rtol=2 ** -6)
 
 
-@pytest.mark.parametrize("hq,hkv,hd,T", [(14, 2, 64, 128), (7, 1, 64, 100), (7, 1, 128, 64)])
-def test_tc_qkv_rope(lib, hq, hkv, hd, T):
+@pytest.mark.parametrize("hq,hkv,hd,T,H", [(14, 2, 64, 128, 896), (7, 1, 64, 100, 896), (7, 1, 128, 64, 896),
+                                          (28, 4, 128, 2048, 256), (8, 2, 32, 300, 256)])
+def test_tc_qkv_rope(lib, hq, hkv, hd, T, H):
     """Prefill QKV projection + bias + RoPE + KV append through the tensor-core path."""
     from minitp_b200 import ops
     from minitp_b200.rope import rope_tables
 
     torch.manual_seed(hq * 10 + hd + T)
-    B, H, cap = 1, 896, 512
+    B, cap = 1, max(512, T + 64)
     x = torch.randn(B, T, H).to(torch.bfloat16)
     w = (torch.randn((hq + 2 * hkv) * hd, H) * 0.05).to(torch.bfloat16)
     b = (torch.randn((hq + 2 * hkv) * hd) * 0.05).to(torch.bfloat16)
