@@ -39,6 +39,7 @@ sys.path.insert(0, REPO)
 
 MEASURED_PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def parse_args(argv=None):
@@ -56,8 +57,11 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-pdl", action="store_true")
     p.add_argument("--out", default=None, help="also write the JSON line here")
-    p.add_argument("--workload", default="decode", choices=["decode", "fused_ar"],
-                   help="decode (default) or the fused AllReduce+residual+RMSNorm microbenchmark")
+    p.add_argument("--workload", default="decode", choices=["decode", "fused_ar", "prefill_gemm"],
+                   help="decode (default), the fused AllReduce+residual+RMSNorm microbenchmark, or the "
+                        "tensor-core prefill GEMM sweep")
+    p.add_argument("--gemm-shapes", default=None,
+                   help="prefill_gemm: comma-separated names of the shapes to run (default: all)")
     p.add_argument("--iters", type=int, default=10000, help="fused_ar: iterations per size")
     return p.parse_args(argv)
 
@@ -81,6 +85,59 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def peak_tflops():
+    """Dense bf16 peak: the burst cuBLAS figure (a GEMM timed alone)."""
+    try:
+        with open(MEASURED_PEAKS) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def time_prefill_gemm(epi: str, M: int, N: int, K: int, dev, reps: int = 20) -> dict:
+    """Device time per launch of the tensor-core GEMM (gemm_tc_kernel).
+
+    `epi` "swiglu" runs ops.linear_swiglu (N = 2 x intermediate rows of W),
+    "store" runs ops.linear. The launches are captured in a CUDA graph so the
+    host does not pace them, and they cycle over enough distinct weight copies
+    (> 256 MiB in all) that every launch reads its weights from HBM, not L2.
+    """
+    from minitp_b200 import ops
+
+    wbytes = N * K * 2
+    copies = max(2, min(64, (256 << 20) // wbytes + 1))
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    ws = [(torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    fn = (lambda w: ops.linear_swiglu(x, w)) if epi == "swiglu" else (lambda w: ops.linear(x, w))
+    for w in ws[:3]:
+        fn(w)  # eager calls set the kernel attributes before capture
+    torch.cuda.synchronize()
+    n = max(reps, copies)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(n):
+            fn(ws[i % copies])
+    graph.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(3):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (3 * n)
+    del graph
+    flops = 2.0 * M * N * K
+    peak, peak_kind = peak_tflops()
+    tflops = flops / (us * 1e-6) / 1e12
+    byts = wbytes + M * K * 2 + M * (N // 2 if epi == "swiglu" else N) * 2
+    return {"bound": "tensor", "kernel": f"gemm_tc_kernel ({epi})", "M": M, "N": N, "K": K,
+            "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+            "peak_kind": peak_kind, "us_per_launch": round(us, 3), "flops_per_launch": flops,
+            "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1), "bytes_per_launch": byts,
+            "timing": f"CUDA graph of {n} launches over {copies} weight copies, CUDA events"}
 
 
 # ---------------------------------------------------------------------- #
@@ -350,6 +407,12 @@ def run_b200(args, cfg, prompt_len, new_tokens):
     k_bytes = w.numel() * w.element_size() + x.numel() * x.element_size() + args.batch * w.shape[0] * w.element_size()
     k_gbs = k_bytes / (k_ms / 1e3) / 1e9
 
+    # the prefill GEMM (tensor cores) at this workload's prefill rows, gate/up shape
+    gu = model.model.layers[0].mlp.gate_up_proj.weight
+    tc_line = None
+    if dtype == torch.bfloat16 and args.batch * prompt_len >= 64:
+        tc_line = time_prefill_gemm("swiglu", args.batch * prompt_len, gu.shape[0], gu.shape[1], dev)
+
     wb = weight_bytes_per_token(model)
     kvb = kv_bytes_per_token(model, args.batch, prompt_len + new_tokens / 2)
     tok_gbs = (wb + kvb) / (ms_per_token / 1e3) / 1e9
@@ -386,6 +449,7 @@ def run_b200(args, cfg, prompt_len, new_tokens):
                               "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
                               "frac": round(k_gbs / peak, 4), "bytes_per_launch": k_bytes,
                               "us_per_launch": round(k_ms * 1e3, 3)},
+            "roofline_prefill_gemm": tc_line,
             "gpu_launches": launches_per_generation(cfg.num_hidden_layers, new_tokens, prompt_len,
                                                     step_launches) * args.steps,
             "clocks": clocks,
@@ -494,10 +558,46 @@ def run_fused_ar(args):
     ctx.destroy()
 
 
+# (name, epilogue, M, N, K): prefill projections of the two model shapes.
+# 0.5B: gate/up (2 x 4864) and down at the 128-token prompt and a 2048-token
+# chunk; 7B at TP=4: QKV, gate/up (2 x 4736) and down at B=1 x 1024 and
+# B=8 x 1024 prompt rows.
+PREFILL_GEMM_SHAPES = [
+    ("05b_gateup_m128", "swiglu", 128, 9728, 896),
+    ("05b_gateup_m2048", "swiglu", 2048, 9728, 896),
+    ("05b_down_m2048", "store", 2048, 896, 4864),
+    ("05b_qkv_m2048", "store", 2048, 1152, 896),
+    ("7b_tp4_qkv_m1024", "store", 1024, 1152, 3584),
+    ("7b_tp4_gateup_m1024", "swiglu", 1024, 9472, 3584),
+    ("7b_tp4_down_m1024", "store", 1024, 3584, 4736),
+    ("7b_tp4_gateup_m8192", "swiglu", 8192, 9472, 3584),
+    ("7b_tp4_down_m8192", "store", 8192, 3584, 4736),
+]
+
+
+def run_prefill_gemm(args):
+    """Tensor-core prefill GEMM sweep on one GPU: one JSON line per shape."""
+    from minitp_b200.build import build
+
+    build()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    want = set(args.gemm_shapes.split(",")) if args.gemm_shapes else None
+    for name, epi, M, N, K in PREFILL_GEMM_SHAPES:
+        if want and name not in want:
+            continue
+        r = time_prefill_gemm(epi, M, N, K, dev)
+        r = {"workload": "prefill_gemm", "shape": name, **r}
+        print(json.dumps(r), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.workload == "fused_ar":
         run_fused_ar(args)
+        return
+    if args.workload == "prefill_gemm":
+        run_prefill_gemm(args)
         return
     cfg, prompt_len, new_tokens = workload(args)
     if args.impl == "reference":

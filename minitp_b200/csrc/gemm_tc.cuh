@@ -108,6 +108,48 @@ __device__ __forceinline__ int tc_col_b(int q, int hd) {
   return BN / 2 + q;
 }
 
+// Epilogue of one output unit (this lane's column) over `rows` rows of a
+// tile: a[r * kTcXs] and b[r * kTcXs] hold row r's accumulator values (the
+// unit's two operands for SwiGLU / RoPE). Store and SwiGLU keep the GEMV
+// epilogue's arithmetic with the per-unit bias loaded once for all rows (so
+// the row iterations are independent and interleave); the other epilogues
+// call the GEMV epilogue per element.
+template <typename T, int EPI>
+__device__ __forceinline__ void tc_epi_rows(const GemvParams& p, int row0, int rows, int unit, const float* a,
+                                            const float* b, uint32_t out_seq) {
+  if constexpr (EPI == kEpiStore) {
+    T* y = static_cast<T*>(p.y) + unit;
+    if (p.bias) {
+      const float bias = to_f(static_cast<const T*>(p.bias)[unit]);
+#pragma unroll 4
+      for (int r = 0; r < rows; ++r) y[size_t(out_row(p, row0 + r)) * p.ldy] = from_f<T>(a[r * kTcXs] + bias);
+    } else {
+#pragma unroll 4
+      for (int r = 0; r < rows; ++r) y[size_t(out_row(p, row0 + r)) * p.ldy] = from_f<T>(a[r * kTcXs]);
+    }
+  } else if constexpr (EPI == kEpiSwiglu) {
+    const int half = p.N >> 1;
+    const bool has_bias = p.bias != nullptr;
+    const float bg = has_bias ? to_f(static_cast<const T*>(p.bias)[unit]) : 0.f;
+    const float bu = has_bias ? to_f(static_cast<const T*>(p.bias)[unit + half]) : 0.f;
+    T* y = static_cast<T*>(p.y) + unit;
+#pragma unroll 4
+    for (int r = 0; r < rows; ++r) {
+      float g = a[r * kTcXs], up = b[r * kTcXs];
+      if (has_bias) {
+        g += bg;
+        up += bu;
+      }
+      g = round_t<T>(g);
+      up = round_t<T>(up);
+      y[size_t(row0 + r) * p.ldy] = from_f<T>(round_t<T>(silu_f(g)) * up);
+    }
+  } else {
+#pragma unroll 2
+    for (int r = 0; r < rows; ++r) gemv_epilogue<T, EPI>(p, row0 + r, unit, a[r * kTcXs], b[r * kTcXs], out_seq, nullptr);
+  }
+}
+
 template <typename T, int EPI, int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const TcParams tp, const __grid_constant__ CUtensorMap map_x,
@@ -253,13 +295,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
         const int unit = u_tile + q0 + lane;
-        for (int r = 0; r < 32; ++r) {
-          const int m = row0 + r;
-          if (m >= p.M) break;
-          const float v0 = bufa[r * kTcXs + lane];
-          const float v1 = kPair ? bufb[r * kTcXs + lane] : 0.f;
-          if (unit < bound) gemv_epilogue<T, EPI>(p, m, unit, v0, v1, out_seq, nullptr);
-        }
+        const int rows = min(32, p.M - row0);
+        if (unit < bound && rows > 0) tc_epi_rows<T, EPI>(p, row0, rows, unit, bufa + lane, bufb + lane, out_seq);
         __syncwarp();
       }
       // the accumulator may be overwritten once every epilogue warp has read it
