@@ -50,6 +50,13 @@ int mtpb_set_gemv_ctas_per_sm(int n);
  * (tcgen05) GEMM instead of the GEMV kernel; a large value keeps them on the GEMV. */
 int mtpb_set_tc_min_rows(int rows);
 
+/* Allow (1, default) or forbid (0) the CTA-pair tensor-core GEMM
+ * (tcgen05 cta_group::2, 256 x 256 tiles on two SMs) for projections of at
+ * least 256 rows; returns the previous setting. With 0, the single-CTA kernel
+ * runs every tensor-core projection. No counterpart in the reference (a
+ * tuning switch of this library). */
+int mtpb_set_tc_pair(int enable);
+
 /* ------------------------------------------------------- communicator
  * Peer-memory communicator over NVLink (one per rank; TP group == world).
  * Replaces the torch.distributed process group used by the hot-path

@@ -219,42 +219,97 @@ int tc_tiles_n(const GemvParams& p, int bn) {
   return (p.N + bn - 1) / bn;
 }
 
-// 256-column tiles when they alone give every SM a tile, else 128 (more CTAs
-// on the small-M, HBM-bound shapes)
+// Launch plan of a tensor-core GEMM: CTA pairs with 256 x 256 tiles when
+// there are at least as many tiles as co-resident pairs, else single CTAs
+// with 128-row tiles 256 columns wide when those alone give every SM a tile,
+// else 128 wide (more CTAs on the small-M, HBM-bound shapes). Persistent
+// grids: one CTA per SM at most.
+struct TcPlan {
+  int pair;  // 1: gemm_tc2_kernel (cta_group::2)
+  int bn;    // single-CTA tile width
+  int tiles_m, tiles_n;
+  int grid;
+};
+
+int g_tc_pair = 1;  // CTA-pair kernel allowed
+
+// Per-epilogue one-time setup: shared-memory limits of the three kernels and
+// the number of co-resident CTA pairs (their shared memory allows one CTA per
+// SM). Done on the first eligible call, which must not be under graph capture.
+struct TcState {
+  bool ready = false;
+  int pairs = 0;
+};
+
 template <int EPI>
-int tc_bn(const GemvParams& p) {
-  const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
-  return tiles_m * tc_tiles_n<EPI>(p, 256) >= sm_count() ? 256 : 128;
+TcState& tc_state() {
+  static TcState s;
+  return s;
 }
 
-// persistent grid: one CTA per SM at most
+template <int EPI>
+int tc_prepare(cudaStream_t st) {
+  TcState& s = tc_state<EPI>();
+  if (s.ready) return MTPB_OK;
+  if (capturing(st)) return fail(MTPB_ERR_INVALID, "tensor-core GEMM: run one call eagerly before graph capture");
+  MTPB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<bf16, EPI, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(TcCfg<128>::kSmem)));
+  MTPB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<bf16, EPI, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(TcCfg<256>::kSmem)));
+  MTPB_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<bf16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kTc2Smem)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * sm_count());
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTc2Smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<bf16, EPI>, &cfg) != cudaSuccess || n < 0) {
+    cudaGetLastError();
+    n = 0;
+  }
+  s.pairs = std::min(n, sm_count() / 2);
+  s.ready = true;
+  return MTPB_OK;
+}
+
+template <int EPI>
+TcPlan tc_plan(const GemvParams& p) {
+  TcPlan pl{};
+  const int pairs = (g_tc_pair && p.M >= 256) ? tc_state<EPI>().pairs : 0;
+  const int tm2 = (p.M + 255) / 256, tn2 = tc_tiles_n<EPI>(p, 256);
+  if (pairs > 0 && tm2 * tn2 >= pairs) {
+    pl.pair = 1;
+    pl.tiles_m = tm2;
+    pl.tiles_n = tn2;
+    pl.grid = 2 * std::min(tm2 * tn2, pairs);
+    return pl;
+  }
+  pl.tiles_m = (p.M + kTcBM - 1) / kTcBM;
+  pl.bn = pl.tiles_m * tc_tiles_n<EPI>(p, 256) >= sm_count() ? 256 : 128;
+  pl.tiles_n = tc_tiles_n<EPI>(p, pl.bn);
+  pl.grid = std::min(pl.tiles_m * pl.tiles_n, sm_count());
+  return pl;
+}
+
 template <int EPI>
 int tc_grid(const GemvParams& p) {
-  const int tiles = tc_tiles_n<EPI>(p, tc_bn<EPI>(p)) * ((p.M + kTcBM - 1) / kTcBM);
-  return std::min(tiles, sm_count());
+  return tc_plan<EPI>(p).grid;
 }
 
-template <int EPI, int BN>
-int gemm_tc_launch_bn(const GemvParams& g, cudaStream_t st) {
-  TcParams tp;
-  tp.g = g;
-  tp.tiles_m = (g.M + kTcBM - 1) / kTcBM;
-  tp.tiles_n = tc_tiles_n<EPI>(g, BN);
-  tp.budget_ns = 2000000000ull;
-  CUtensorMap mx, mw;
-  MTPB_TRY(make_map_bf16(&mx, g.x, uint64_t(g.M), uint64_t(g.K), uint64_t(g.ldx), kTcBM));
-  MTPB_TRY(make_map_bf16(&mw, g.w, uint64_t(g.N), uint64_t(g.K), uint64_t(g.K), EPI == kEpiSwiglu ? BN / 2 : BN));
-  auto kern = gemm_tc_kernel<bf16, EPI, BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (capturing(st)) return fail(MTPB_ERR_INVALID, "tensor-core GEMM: run one call eagerly before graph capture");
-    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TcCfg<BN>::kSmem)));
-    attr_set = true;
-  }
+template <typename K>
+int tc_launch_kernel(K kern, const TcPlan& pl, size_t smem, const TcParams& tp, const CUtensorMap& mx,
+                     const CUtensorMap& mw, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min(tp.tiles_m * tp.tiles_n, sm_count()));
+  cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -267,7 +322,21 @@ int gemm_tc_launch_bn(const GemvParams& g, cudaStream_t st) {
 
 template <int EPI>
 int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
-  return tc_bn<EPI>(g) == 256 ? gemm_tc_launch_bn<EPI, 256>(g, st) : gemm_tc_launch_bn<EPI, 128>(g, st);
+  MTPB_TRY(tc_prepare<EPI>(st));
+  const TcPlan pl = tc_plan<EPI>(g);
+  TcParams tp;
+  tp.g = g;
+  tp.tiles_m = pl.tiles_m;
+  tp.tiles_n = pl.tiles_n;
+  tp.budget_ns = 2000000000ull;
+  // W boxes: a CTA of a pair loads 128 rows; a single CTA BN rows (SwiGLU: two halves)
+  const uint32_t wbox = pl.pair ? 128u : uint32_t(EPI == kEpiSwiglu ? pl.bn / 2 : pl.bn);
+  CUtensorMap mx, mw;
+  MTPB_TRY(make_map_bf16(&mx, g.x, uint64_t(g.M), uint64_t(g.K), uint64_t(g.ldx), kTcBM));
+  MTPB_TRY(make_map_bf16(&mw, g.w, uint64_t(g.N), uint64_t(g.K), uint64_t(g.K), wbox));
+  if (pl.pair) return tc_launch_kernel(gemm_tc2_kernel<bf16, EPI>, pl, kTc2Smem, tp, mx, mw, st);
+  if (pl.bn == 256) return tc_launch_kernel(gemm_tc_kernel<bf16, EPI, 256>, pl, TcCfg<256>::kSmem, tp, mx, mw, st);
+  return tc_launch_kernel(gemm_tc_kernel<bf16, EPI, 128>, pl, TcCfg<128>::kSmem, tp, mx, mw, st);
 }
 
 template <int EPI>
@@ -1384,6 +1453,12 @@ int mtpb_set_tc_min_rows(int rows) {
   if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
   g_tc_min_rows = rows;
   return MTPB_OK;
+}
+
+int mtpb_set_tc_pair(int enable) {
+  const int prev = g_tc_pair;
+  g_tc_pair = enable ? 1 : 0;
+  return prev;
 }
 
 int mtpb_set_decode_spin(int backoff_ns) {

@@ -150,6 +150,39 @@ __device__ __forceinline__ void tc_epi_rows(const GemvParams& p, int row0, int r
   }
 }
 
+// One epilogue warp's share of a finished accumulator: tile-local units
+// [part * U/2, (part + 1) * U/2) of rows row0 .. row0 + 31, where trow is the
+// tensor-memory address of the warp's lane quarter in the accumulator, U the
+// units per tile and u_tile the first unit of the tile.
+template <typename T, int EPI, int BN>
+__device__ __forceinline__ void tc_epilogue_tile(const GemvParams& p, uint32_t trow, int row0, int u_tile, int part,
+                                                 float* bufa, float* bufb, int lane, uint32_t out_seq) {
+  constexpr bool kPair = EPI == kEpiSwiglu || EPI == kEpiRope;
+  constexpr int kUnitsPerTile = kPair ? BN / 2 : BN;
+  const int hd = p.hd;
+  const int bound = EPI == kEpiSwiglu ? (p.N >> 1) : EPI == kEpiRope ? (p.hq + 2 * p.hkv) * (hd >> 1) : p.N;
+  for (int q0 = part * (kUnitsPerTile / 2); q0 < (part + 1) * (kUnitsPerTile / 2); q0 += 32) {
+    uint32_t ra[32], rb[32];
+    tc_ld16(trow + tc_col_a<EPI, BN>(q0, hd), ra);
+    tc_ld16(trow + tc_col_a<EPI, BN>(q0 + 16, hd), ra + 16);
+    if constexpr (kPair) {
+      tc_ld16(trow + tc_col_b<EPI, BN>(q0, hd), rb);
+      tc_ld16(trow + tc_col_b<EPI, BN>(q0 + 16, hd), rb + 16);
+    }
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      bufa[lane * kTcXs + j] = __uint_as_float(ra[j]);
+      if constexpr (kPair) bufb[lane * kTcXs + j] = __uint_as_float(rb[j]);
+    }
+    __syncwarp();
+    const int unit = u_tile + q0 + lane;
+    const int rows = min(32, p.M - row0);
+    if (unit < bound && rows > 0) tc_epi_rows<T, EPI>(p, row0, rows, unit, bufa + lane, bufb + lane, out_seq);
+    __syncwarp();
+  }
+}
+
 template <typename T, int EPI, int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const TcParams tp, const __grid_constant__ CUtensorMap map_x,
@@ -264,8 +297,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;
     float* bufa = xpose + size_t(ew) * (2 * 32 * kTcXs);
     float* bufb = bufa + 32 * kTcXs;
-    const int hd = p.hd;
-    const int bound = EPI == kEpiSwiglu ? (p.N >> 1) : EPI == kEpiRope ? (p.hq + 2 * p.hkv) * (hd >> 1) : p.N;
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int b = i & 1, use = i >> 1;
@@ -277,28 +308,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_after();
       const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * BN);
-      const int row0 = tm * kTcBM + quarter * 32;
-      const int u_tile = tn * kUnitsPerTile;
-      for (int q0 = part * (kUnitsPerTile / 2); q0 < (part + 1) * (kUnitsPerTile / 2); q0 += 32) {
-        uint32_t ra[32], rb[32];
-        tc_ld16(trow + tc_col_a<EPI, BN>(q0, hd), ra);
-        tc_ld16(trow + tc_col_a<EPI, BN>(q0 + 16, hd), ra + 16);
-        if constexpr (kPair) {
-          tc_ld16(trow + tc_col_b<EPI, BN>(q0, hd), rb);
-          tc_ld16(trow + tc_col_b<EPI, BN>(q0 + 16, hd), rb + 16);
-        }
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          bufa[lane * kTcXs + j] = __uint_as_float(ra[j]);
-          if constexpr (kPair) bufb[lane * kTcXs + j] = __uint_as_float(rb[j]);
-        }
-        __syncwarp();
-        const int unit = u_tile + q0 + lane;
-        const int rows = min(32, p.M - row0);
-        if (unit < bound && rows > 0) tc_epi_rows<T, EPI>(p, row0, rows, unit, bufa + lane, bufb + lane, out_seq);
-        __syncwarp();
-      }
+      tc_epilogue_tile<T, EPI, BN>(p, trow, tm * kTcBM + quarter * 32, tn * kUnitsPerTile, part, bufa, bufb, lane,
+                                   out_seq);
       // the accumulator may be overwritten once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
@@ -325,6 +336,234 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of two CTAs on two SMs computes
+// a 256 x 256 output tile. Each CTA loads its own 128 rows of x and half of
+// the tile's W rows (128) per K block, so an SM takes in 32 KB per 128 x 256 x
+// 64 block of MMAs instead of 48 KB; the leader CTA (cluster rank 0) issues
+// tcgen05.mma.cta_group::2 (M 256, N 256), which reads A and B from both
+// CTAs' shared memory and accumulates rows 0-127 in the leader's tensor
+// memory and rows 128-255 in the peer's. Both CTAs' TMA loads (no multicast)
+// complete on the leader's stage barrier; the leader's commits arrive on the
+// barriers of both CTAs; the peer's epilogue warps release an accumulator on
+// the leader's barrier. Before either CTA frees its tensor memory or exits,
+// every stage it loaded has been consumed by the MMAs and a cluster barrier
+// has been passed, so no copy, MMA or remote arrive targets a finished CTA.
+// ---------------------------------------------------------------------------
+constexpr int kTc2Stages = 4;
+constexpr uint32_t kTc2StageBytes = 2 * kTcABytes;  // own x tile + own half of the W tile
+constexpr size_t kTc2Smem = size_t(kTc2Stages) * kTc2StageBytes + size_t(kTcEpiWarps) * kTcXposeBytes + 1024;
+constexpr uint32_t kTc2Idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(256 >> 3) << 17) | (uint32_t(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-D TMA load into this CTA's shared memory completing on a barrier of either
+// CTA of the pair (no multicast)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc2_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(da), "l"(db), "r"(kTc2Idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the barrier at this offset in both CTAs once the MMAs issued so far complete
+__device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc2_commit_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+template <typename T, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    gemm_tc2_kernel(const TcParams tp, const __grid_constant__ CUtensorMap map_x,
+                    const __grid_constant__ CUtensorMap map_w) {
+  constexpr int BN = 256;
+  constexpr int S = kTc2Stages;
+  constexpr bool kPair = EPI == kEpiSwiglu || EPI == kEpiRope;
+  constexpr int kUnitsPerTile = kPair ? BN / 2 : BN;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t full[S], empty[S], acc_full[2], acc_empty[2], drain;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_sh;
+  volatile int* abort = &abort_sh;
+  const GemvParams& p = tp.g;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  float* xpose = reinterpret_cast<float*>(smem_raw + (base - smem_u32(smem_raw)) + size_t(S) * kTc2StageBytes);
+  const int nk = (p.K + kTcBK - 1) / kTcBK;
+  const int tiles = tp.tiles_m * tp.tiles_n;  // 256 x 256 tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);   // the leader's expect-tx arrive (+ both CTAs' bytes)
+      mbar_init(empty + s, 1);  // the leader's MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 2 * kTcEpiWarps);  // epilogue warps of both CTAs
+    }
+    mbar_init(&drain, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers and tensor memory exist before any copy or MMA
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  pdl_launch();
+  pdl_wait();
+
+  uint32_t out_seq = 0;
+  if constexpr (EPI == kEpiPush) out_seq = resolve_seq(p.comm, p.out_seq);
+  int issued = 0;
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs): own x rows and own half of the W rows
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_rank(smem_u32(full), 0);
+      int g = 0;
+      for (int t = cid; t < tiles && !*abort; t += ncl) {
+        const int tm = t % tp.tiles_m, tn = t / tp.tiles_m;
+        int wrow;
+        if constexpr (EPI == kEpiSwiglu) {
+          wrow = tn * (BN / 2) + (crank ? (p.N >> 1) : 0);  // gate rows in the leader, up rows in the peer
+        } else {
+          wrow = tn * BN + int(crank) * (BN / 2);
+        }
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % S;
+          if (g >= S && !mbar_wait(empty + s, uint32_t((g / S) & 1) ^ 1u, tp.budget_ns, abort)) {
+            *abort = 1;
+            break;
+          }
+          if (*abort) break;
+          const uint32_t sa = base + uint32_t(s) * kTc2StageBytes, sb = sa + kTcABytes;
+          if (leader) mbar_arrive_expect_tx(full + s, 2 * kTc2StageBytes);
+          tma_load_2d_pair(sa, &map_x, kb * kTcBK, tm * 256 + int(crank) * kTcBM, full_leader + 8u * uint32_t(s));
+          tma_load_2d_pair(sb, &map_w, kb * kTcBK, wrow, full_leader + 8u * uint32_t(s));
+          issued = g + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int g = 0, i = 0;
+      for (int t = cid; t < tiles && !*abort; t += ncl, ++i) {
+        const int b = i & 1, use = i >> 1;
+        if (use > 0 && !mbar_wait(acc_empty + b, uint32_t((use - 1) & 1), tp.budget_ns, abort)) {
+          *abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + uint32_t(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(full + s, uint32_t((g / S) & 1), tp.budget_ns, abort)) {
+            *abort = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + uint32_t(s) * kTc2StageBytes, sb = sa + kTcABytes;
+#pragma unroll
+          for (int k = 0; k < kTcBK / 16; ++k)
+            tc2_mma(acc, tc_smem_desc(sa + k * 32), tc_smem_desc(sb + k * 32), (kb > 0 || k > 0) ? 1u : 0u);
+          tc2_commit_both(empty + s);  // both CTAs' stage s is free once these MMAs have read it
+        }
+        if (!ok) break;
+        tc2_commit_both(acc_full + b);
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
+    const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;
+    float* bufa = xpose + size_t(ew) * (2 * 32 * kTcXs);
+    float* bufb = bufa + 32 * kTcXs;
+    const uint32_t acc_empty_leader = mapa_rank(smem_u32(acc_empty), 0);
+    int i = 0;
+    for (int t = cid; t < tiles; t += ncl, ++i) {
+      const int b = i & 1, use = i >> 1;
+      const int tm = t % tp.tiles_m, tn = t / tp.tiles_m;
+      const bool ok = mbar_wait(acc_full + b, uint32_t(use & 1), tp.budget_ns, abort);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) *abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * BN);
+      tc_epilogue_tile<T, EPI, BN>(p, trow, tm * 256 + int(crank) * kTcBM + quarter * 32, tn * kUnitsPerTile, part,
+                                   bufa, bufb, lane, out_seq);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8u * uint32_t(b));
+    }
+  }
+  __syncwarp();
+  if constexpr (EPI == kEpiPush) signal_peers(p.comm, p.out_chan, out_seq);
+
+  // ---- teardown
+  if (warp == 0 && lane == 0) {
+    // every stage this CTA loaded has been read by the MMAs (so its copies landed)
+    int never = 0;
+    for (int g = max(0, issued - S); g < issued; ++g)
+      mbar_wait(empty + (g % S), uint32_t((g / S) & 1), tp.budget_ns, &never);
+  }
+  if (warp == 1 && lane == 0 && leader) {
+    int never = 0;
+    tc2_commit_local(&drain);  // completes once every MMA this thread issued has
+    mbar_wait(&drain, 0u, tp.budget_ns, &never);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer is done with this CTA's memory
+  if (threadIdx.x == 0 && *abort) atomicOr(p.comm.status(), kStatusTimeout);
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
   }
 }
 

@@ -4,8 +4,10 @@ bf16 projections with at least 64 rows run on the tensor-core kernel
 (gemm_tc.cuh); these tests pin its output against a float64 reference of the
 same bf16 inputs, with the store, SwiGLU and fused QKV + RoPE + KV-append
 epilogues, full and partial tiles, K that is not a multiple of the 64-element
-K block, both tile widths (128 and 256 accumulator columns) and persistent
-CTAs that take several tiles each (both tensor-memory accumulators in turn).
+K block, both tile widths of the single-CTA kernel (128 and 256 accumulator
+columns), the CTA-pair kernel (256 x 256 tiles, cta_group::2: projections of
+>= 256 rows with at least one tile per co-resident pair), and persistent CTAs
+that take several tiles each (both tensor-memory accumulators in turn).
 """
 
 import pytest
@@ -24,7 +26,8 @@ def _ref_linear(x, w, b=None):
 
 @pytest.mark.parametrize("M,N,K", [(64, 128, 64), (128, 1152, 896), (200, 300, 896), (128, 896, 4864),
                                    (256, 640, 1000), (130, 4096, 896),
-                                   (2048, 9728, 896), (1152, 2304, 512), (300, 20000, 128)])
+                                   (2048, 9728, 896), (1152, 2304, 512), (300, 20000, 128),
+                                   (200, 40000, 64)])
 def test_tc_linear(lib, M, N, K):
     from minitp_b200 import ops
 
@@ -88,3 +91,22 @@ def test_tc_qkv_rope(lib, hq, hkv, hd, T, H):
     torch.testing.assert_close(kcg.cpu()[:, :, :T].float(), ko.float(), **tol)
     torch.testing.assert_close(vcg.cpu()[:, :, :T].float(), vo.float(), **tol)
     assert torch.equal(kcg.cpu()[:, :, T:], kc[:, :, T:])
+
+
+@pytest.mark.parametrize("epi,M,N,K", [("store", 2048, 9728, 896), ("swiglu", 1024, 9728, 896),
+                                       ("store", 768, 20480, 320), ("swiglu", 300, 20000, 128)])
+def test_tc_pair_matches_single_cta(lib, epi, M, N, K):
+    """The CTA-pair kernel and the single-CTA kernel agree on the same inputs."""
+    from minitp_b200 import ops
+
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    fn = ops.linear_swiglu if epi == "swiglu" else ops.linear
+    y_pair = fn(x, w).cpu()
+    prev = lib.mtpb_set_tc_pair(0)
+    try:
+        y_single = fn(x, w).cpu()
+    finally:
+        lib.mtpb_set_tc_pair(prev)
+    torch.testing.assert_close(y_pair.float(), y_single.float(), atol=1e-3, rtol=2 ** -7)
