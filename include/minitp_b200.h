@@ -269,6 +269,13 @@ int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags);
  * that has not arrived yet (0, the default: poll back to back). */
 int mtpb_set_decode_spin(int backoff_ns);
 
+/* Counter bumped by every mtpb_set_* call. A CUDA graph captured over this
+ * library's calls keeps the settings in force at capture; a holder of such a
+ * graph (the Python generation loop keeps one per shape) compares this value
+ * with the one at capture and recaptures when it changed. No counterpart in
+ * the reference. */
+uint64_t mtpb_settings_epoch(void);
+
 #ifdef __cplusplus
 }
 #endif

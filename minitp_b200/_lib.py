@@ -109,6 +109,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_set_decode_trace": (c_int, [c_void_p]),
     "mtpb_set_decode_ring": (c_int, [c_int, c_int, c_int]),
     "mtpb_set_decode_spin": (c_int, [c_int]),
+    "mtpb_settings_epoch": (c_uint64, []),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1074,19 +1075,26 @@ int model_forward(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
 // =====================================================================
 // extern "C"
 // =====================================================================
+// Bumped by every mtpb_set_* call: a CUDA graph captured over the library
+// bakes in the settings of its capture, so holders of a graph compare epochs.
+std::atomic<uint64_t> g_settings_epoch{0};
+
 extern "C" {
 
 const char* mtpb_last_error(void) { return g_err.c_str(); }
 int mtpb_version(void) { return 1; }
 int mtpb_set_pdl(int enable) {
+  g_settings_epoch.fetch_add(1);
   g_pdl = enable != 0;
   return MTPB_OK;
 }
 int mtpb_set_prefetch_cap(uint32_t bytes) {
+  g_settings_epoch.fetch_add(1);
   g_prefetch_cap = bytes;
   return MTPB_OK;
 }
 int mtpb_set_gemv_ctas_per_sm(int n) {
+  g_settings_epoch.fetch_add(1);
   if (n < 1 || n > 8) return fail(MTPB_ERR_INVALID, "gemv CTAs per SM must be in [1, 8]");
   g_gemv_ctas_per_sm = n;
   return MTPB_OK;
@@ -1439,6 +1447,7 @@ int mtpb_model_destroy(void* model) {
 }
 
 int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
+  g_settings_epoch.fetch_add(1);
   if (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4 || lm_chunk_kb < 4 || lm_chunk_kb > 200 || lm_chunk_kb % 4)
     return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4");
   if (l2_flags < 0 || l2_flags > 3) return fail(MTPB_ERR_INVALID, "decode ring: l2 flags 0..3");
@@ -1450,33 +1459,40 @@ int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
 }
 
 int mtpb_set_tc_min_rows(int rows) {
+  g_settings_epoch.fetch_add(1);
   if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
   g_tc_min_rows = rows;
   return MTPB_OK;
 }
 
 int mtpb_set_tc_pair(int enable) {
+  g_settings_epoch.fetch_add(1);
   const int prev = g_tc_pair;
   g_tc_pair = enable ? 1 : 0;
   return prev;
 }
 
 int mtpb_set_decode_spin(int backoff_ns) {
+  g_settings_epoch.fetch_add(1);
   if (backoff_ns < 0 || backoff_ns > 100000) return fail(MTPB_ERR_INVALID, "decode spin back-off: 0 .. 100000 ns");
   g_mk_spin_ns = uint32_t(backoff_ns);
   return MTPB_OK;
 }
 
 int mtpb_set_decode_trace(void* buf) {
+  g_settings_epoch.fetch_add(1);
   g_mk_trace = static_cast<unsigned long long*>(buf);
   return MTPB_OK;
 }
 
 int mtpb_set_decode_impl(int impl) {
+  g_settings_epoch.fetch_add(1);
   if (impl != 0 && impl != 1) return fail(MTPB_ERR_INVALID, "decode impl must be 0 (megakernel) or 1 (kernel chain)");
   g_decode_impl = impl;
   return MTPB_OK;
 }
+
+uint64_t mtpb_settings_epoch(void) { return g_settings_epoch.load(); }
 
 int mtpb_model_forward(void* model, const int64_t* ids, int B, int T, const int64_t* rope_pos, int cache_len,
                        void* const* k_caches, void* const* v_caches, int cap, void* logits, int last_only,

@@ -44,6 +44,48 @@ def select_token(model: TPQwen2ForCausalLM, logits: torch.Tensor, distributed_ar
     return ops.argmax(full, 0, None).squeeze(-1)
 
 
+class DecodeSession:
+    """Buffers of one (batch, total length) shape kept on the model between
+    ``generate_greedy`` calls: the KV cache, the output ids, the positions,
+    the device token, and the CUDA graph of the decode step captured over
+    them. A later call of the same shape replays that graph instead of
+    running an eager step and capturing a new graph (a few ms per call).
+    Sessions are dropped whenever the model's native handle is released.
+    """
+
+    def __init__(self, model: TPQwen2ForCausalLM, batch: int, total: int, device: torch.device, native: int) -> None:
+        self.kv = make_kv_cache(model, batch, total)
+        self.out_ids = torch.empty(batch, total, dtype=torch.long, device=device)
+        self.positions = torch.arange(total, device=device)
+        self.tok = torch.empty(batch, dtype=torch.int64, device=device)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.graph_epoch = -1  # library settings epoch at the graph's capture
+        self.native = native  # handle of the native model the graph runs
+
+    def usable_graph(self) -> torch.cuda.CUDAGraph | None:
+        """The captured graph, unless a library setting changed since its capture."""
+        if self.graph is not None and self.graph_epoch != _lib.load().mtpb_settings_epoch():
+            self.graph = None
+        return self.graph
+
+
+_MAX_SESSIONS = 4
+
+
+def decode_session(model: TPQwen2ForCausalLM, batch: int, total: int, device: torch.device) -> DecodeSession:
+    """The model's session for this shape (created on first use; at most four kept)."""
+    native = model.native()  # first: (re)building the native model drops the model's sessions
+    cache = model.__dict__.setdefault("_decode_sessions", {})
+    key = (batch, total, str(device))
+    s = cache.pop(key, None)
+    if s is None or s.native != native:
+        s = DecodeSession(model, batch, total, device, native)
+    cache[key] = s  # most recently used last
+    while len(cache) > _MAX_SESSIONS:
+        cache.pop(next(iter(cache)))
+    return s
+
+
 class GenerationState:
     """KV cache + positions buffer + output buffer (reference generation.py:70-130)."""
 
@@ -55,6 +97,7 @@ class GenerationState:
         kv: KVCache | None = None,
         distributed_argmax: bool = True,
         kv_init: str = "empty",
+        session: DecodeSession | None = None,
     ) -> None:
         self.model = model
         self.distributed_argmax = distributed_argmax
@@ -63,11 +106,18 @@ class GenerationState:
         self.prompt_len = t
         self.max_new_tokens = max_new_tokens
         self.total = t + max_new_tokens
-        self.kv = kv if kv is not None else make_kv_cache(model, b, self.total, init=kv_init)
         device = input_ids.device
-        self.out_ids = torch.empty(b, self.total, dtype=torch.long, device=device)
+        self._session = session
+        if session is not None:
+            self.kv = session.kv
+            self.kv.seq_len = 0
+            self.out_ids = session.out_ids
+            self.positions_buf = session.positions
+        else:
+            self.kv = kv if kv is not None else make_kv_cache(model, b, self.total, init=kv_init)
+            self.out_ids = torch.empty(b, self.total, dtype=torch.long, device=device)
+            self.positions_buf = torch.arange(self.total, device=device)
         self.out_ids[:, :t] = input_ids
-        self.positions_buf = torch.arange(self.total, device=device)
         self.cursor = t
         self.finished: torch.Tensor | None = None
         self.eos = -1
@@ -104,7 +154,12 @@ class GenerationState:
         if self.batch > 64:
             raise ValueError("device decode supports at most 64 rows")
         comm = self.model.ctx.comm()
-        self._tok = tok.to(torch.int64).contiguous().clone()
+        if self._session is not None:
+            self._tok = self._session.tok
+            self._tok.copy_(tok.to(torch.int64))
+            self._graph = self._session.usable_graph()
+        else:
+            self._tok = tok.to(torch.int64).contiguous().clone()
         _lib.call("mtpb_comm_set_pos", comm.handle, self.cursor - 1, _lib.stream_ptr(self._tok.device))
         h = self.model.native()
         _lib.call("mtpb_model_reserve", h, self.batch, self.kv.max_seq_len)
@@ -123,6 +178,9 @@ class GenerationState:
         with torch.cuda.graph(g):
             _lib.call("mtpb_model_decode_step", *args, _lib.stream_ptr(self._tok.device))
         self._graph = g
+        if self._session is not None:
+            self._session.graph = g
+            self._session.graph_epoch = _lib.load().mtpb_settings_epoch()
 
     def graph_step(self) -> None:
         self.kv.check_room(1)
@@ -139,6 +197,10 @@ class GenerationState:
         if steps <= 0:
             return self.out_ids
         self.start_device_decode(tok)
+        if use_graph and self._graph is not None:  # a session's graph of this shape
+            for _ in range(steps):
+                self.graph_step()
+            return self.out_ids
         self.device_step()  # first step eagerly: sets function attributes, validates the chain
         if steps > 1:
             if use_graph:
@@ -207,18 +269,24 @@ def generate_greedy(
     rows hit EOS when ``early_stop=True``; exactly prompt + max_new_tokens
     columns otherwise.
     """
-    state = GenerationState(model, input_ids, max_new_tokens, kv=kv, distributed_argmax=distributed_argmax,
-                            kv_init=kv_init)
     b = input_ids.shape[0]
     fixed = not (early_stop and eos_token_id is not None)
     if distributed_argmax and b <= 64:
+        # device decode loop: replays of one captured step, buffers kept per shape
+        session = None
+        if kv is None and kv_init == "empty":
+            session = decode_session(model, b, input_ids.shape[1] + max_new_tokens, input_ids.device)
+        state = GenerationState(model, input_ids, max_new_tokens, kv=kv, distributed_argmax=distributed_argmax,
+                                kv_init=kv_init, session=session)
         if fixed:
             out = state.run_fixed(use_graph=True)
             out = out if not early_stop else out[:, : state.cursor]
         else:
             out = state.run_until_eos(eos_token_id, use_graph=True)
         state.release()
-        return out
+        return out.clone() if session is not None else out
+    state = GenerationState(model, input_ids, max_new_tokens, kv=kv, distributed_argmax=distributed_argmax,
+                            kv_init=kv_init)
     if early_stop and eos_token_id is not None:
         state.eos = eos_token_id
         state.finished = torch.zeros(b, dtype=torch.bool, device=input_ids.device)
@@ -237,4 +305,4 @@ def generate_greedy(
     return state.out_ids[:, : state.cursor] if early_stop else state.out_ids
 
 
-__all__ = ["GenerationState", "generate_greedy", "make_kv_cache", "select_token"]
+__all__ = ["DecodeSession", "GenerationState", "decode_session", "generate_greedy", "make_kv_cache", "select_token"]

@@ -145,6 +145,8 @@ class TPQwen2ForCausalLM(nn.Module):
         return self._native_handle
 
     def release_native(self) -> None:
+        # decode sessions hold graphs captured over the native model's buffers
+        self.__dict__.pop("_decode_sessions", None)
         if self._native_handle is not None:
             torch.cuda.synchronize(self.model.embed_tokens.weight.device)
             _lib.load().mtpb_model_destroy(self._native_handle)

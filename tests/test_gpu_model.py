@@ -221,3 +221,35 @@ def test_kv_overflow_raises(lib):
 def test_status_clean_after_runs(lib):
     for (name, dt), m in list(_MODELS.items()):
         assert m.ctx.comm().status() == 0
+
+
+def test_decode_session_reuse(lib):
+    """Repeated generate_greedy calls of one shape replay the session's graph.
+
+    The second and third calls reuse the buffers and the captured decode step
+    of the first; their ids equal a fresh sessionless run (eager first step and
+    a new capture). A library setting changed after the capture makes the next
+    call capture again.
+    """
+    from minitp_b200.generation import GenerationState, decode_session, generate_greedy
+
+    model = _model("q05b", "bf16")
+    g = golden("model_q05b_tp1_bf16.npz")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    ids2 = torch.randint(0, 151936, tuple(ids.shape), generator=torch.Generator().manual_seed(5)).cuda()
+    n = 20
+    a = generate_greedy(model, ids, n, early_stop=False)
+    sess = decode_session(model, 1, ids.shape[1] + n, ids.device)
+    graph = sess.graph
+    assert graph is not None
+    b = generate_greedy(model, ids2, n, early_stop=False)
+    assert sess.graph is graph
+    a2 = generate_greedy(model, ids, n, early_stop=False)
+    assert torch.equal(a, a2)
+    st = GenerationState(model, ids2, n)
+    fresh = st.run_fixed().clone()
+    st.release()
+    assert torch.equal(b, fresh)
+    lib.mtpb_set_decode_impl(0)  # any setter call moves the settings epoch
+    generate_greedy(model, ids, n, early_stop=False)
+    assert sess.graph is not graph
