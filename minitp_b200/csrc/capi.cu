@@ -588,7 +588,7 @@ struct ModelHost {
 
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
-int g_mk_slot_kb = 96, g_mk_lm_kb = 48, g_mk_l2hint = 1, g_mk_l2ahead = 1;
+int g_mk_slot_kb = 128, g_mk_lm_kb = 96, g_mk_l2hint = 1, g_mk_l2ahead = 1;
 uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
@@ -922,35 +922,43 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
     int K, units, rpu, halves, hoff;
     size_t pre;
   };
+  // LM head: kMkLmRows rows a quarter of the shard apart per unit when they divide it
+  const int vloc = int(d.vocab_end - d.vocab_start);
+  const int lmq = vloc % kMkLmRows == 0 ? kMkLmRows : 1;
   const KindShape ks[kMkKinds] = {
       {d.hidden, int(nq) / P, P, 1, 0, hvec + mk_align(nq * tsz)},  // QKV (+ ln1, bias)
       {d.hq_local * hd, d.hidden / P, P, 1, 0, 0},                  // O
       {d.hidden, d.inter_local / P, P, 2, d.inter_local, hvec},     // gate/up (+ ln2)
       {d.inter_local, d.hidden / P, P, 1, 0, 0},                    // down
-      {d.hidden, int(d.vocab_end - d.vocab_start), 1, 1, 0, hvec},  // LM head (+ final norm)
+      {d.hidden, vloc / lmq, 1, lmq, vloc / lmq, hvec},            // LM head (+ final norm)
   };
-  size_t biggest = 0;
-  for (int k = 0; k < kMkKinds; ++k) {
-    MkKind& kd = p.kinds[k];
-    kd.K = ks[k].K;
-    kd.rpu = ks[k].rpu;
-    kd.halves = ks[k].halves;
-    kd.hoff = ks[k].hoff;
-    kd.base = ks[k].units / G;
-    kd.rem = ks[k].units % G;
-    kd.pre = int(ks[k].pre);
-    const size_t ub = size_t(kd.halves) * kd.rpu * kd.K * tsz;
-    // the LM head streams in smaller chunks: more of them in flight
-    const size_t cmax = k == kMkLm ? size_t(g_mk_lm_kb) * 1024 : chunk_max;
-    const size_t room = cmax > ks[k].pre ? cmax - ks[k].pre : 0;
-    kd.upc = int(std::max<size_t>(1, room / ub));
-    biggest = std::max(biggest, ks[k].pre + size_t(kd.upc) * ub);
-  }
-  // the ring takes the rest of shared memory; it must hold the biggest chunk
+  // the ring takes the rest of shared memory and must hold the biggest
+  // chunk: the layer chunk cap shrinks (16 KiB steps) until it does
   const int budget = smem_optin() - 4096;  // static shared memory of the kernel
   p.ring_bytes = 0;
   const size_t fixed = mk_layout(p, tsz).ring;
-  if (fixed + biggest > size_t(budget)) return kNotEligible;
+  size_t biggest = 0;
+  for (size_t cap = chunk_max;; cap -= 16 * 1024) {
+    biggest = 0;
+    for (int k = 0; k < kMkKinds; ++k) {
+      MkKind& kd = p.kinds[k];
+      kd.K = ks[k].K;
+      kd.rpu = ks[k].rpu;
+      kd.halves = ks[k].halves;
+      kd.hoff = ks[k].hoff;
+      kd.base = ks[k].units / G;
+      kd.rem = ks[k].units % G;
+      kd.pre = int(ks[k].pre);
+      const size_t ub = size_t(kd.halves) * kd.rpu * kd.K * tsz;
+      // the LM head streams in smaller chunks: more of them in flight
+      const size_t cmax = k == kMkLm ? std::min(cap, size_t(g_mk_lm_kb) * 1024) : cap;
+      const size_t room = cmax > ks[k].pre ? cmax - ks[k].pre : 0;
+      kd.upc = int(std::max<size_t>(1, room / ub));
+      biggest = std::max(biggest, ks[k].pre + size_t(kd.upc) * ub);
+    }
+    if (fixed + biggest <= size_t(budget)) break;
+    if (cap <= 16 * 1024) return kNotEligible;
+  }
   p.ring_bytes = int((size_t(budget) - fixed) & ~size_t(127));
   p.l2_hint = g_mk_l2hint;
   p.l2_ahead = g_mk_l2ahead;

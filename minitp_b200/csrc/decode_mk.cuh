@@ -55,6 +55,9 @@ constexpr int kMkSplit = 32;      // KV positions per attention item (one per la
 constexpr int kMkMaxSplits = 64;  // the split merge holds two splits per lane
 constexpr int kMkMaxStage = 16;   // attention items per CTA (all staged in shared memory)
 constexpr int kMkChan = 2;        // communicator channel of the AllReduce sites
+// LM-head rows a warp streams at once: a unit is rows {u, u + V/4, u + V/2,
+// u + 3V/4} of the shard when its vocabulary divides by 4 (else one row)
+constexpr int kMkLmRows = 4;
 constexpr int kMkHdr = 1024;      // shared-memory header: mbarriers + control words
 // Copies of the words that every CTA reads (merged attention output, act):
 // CTA b reads copy b % kMkRep, so fewer CTAs poll any one line.
@@ -1102,14 +1105,24 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
       const bool nan_wins = cm.world == 1;
       const int vloc = int(p.vend - p.vstart);
       T* lg = static_cast<T*>(p.logits);
-      run_kind(kMkLm, int(off), xnorm, H, I1{}, I1{}, [&](int m, int u, const float* v) {
-        const float x = round_t<T>(v[0]);
+      auto lm_row = [&](int m, int u, float v) {
+        const float x = round_t<T>(v);
         if (lg) lg[size_t(m) * vloc + u] = from_f<T>(x);
         const long long pk = argmax_pack(x, uint32_t(p.vstart) + uint32_t(u), nan_wins);
 #pragma unroll
         for (int mm = 0; mm < kMkMaxM; ++mm)
           if (mm == m) best[mm] = pk > best[mm] ? pk : best[mm];
-      });
+      };
+      if (p.kinds[kMkLm].halves == kMkLmRows) {
+        const int q = p.kinds[kMkLm].hoff;
+        run_kind(kMkLm, int(off), xnorm, H, std::integral_constant<int, kMkLmRows>{}, I1{},
+                 [&](int m, int u, const float* v) {
+#pragma unroll
+                   for (int r = 0; r < kMkLmRows; ++r) lm_row(m, r * q + u, v[r]);
+                 });
+      } else {
+        run_kind(kMkLm, int(off), xnorm, H, I1{}, I1{}, [&](int m, int u, const float* v) { lm_row(m, u, v[0]); });
+      }
 #pragma unroll
       for (int m = 0; m < kMkMaxM; ++m) {
         const long long b = warp_max_ll(best[m]);
