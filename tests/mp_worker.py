@@ -22,6 +22,23 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def free_port() -> int:
+    """A port for the rendezvous store, below Linux's ephemeral range (32768+).
+
+    An ephemeral port found free here can be taken by another socket (NCCL's
+    bootstrap uses ephemeral ports) before rank 0 binds it; ports outside that
+    range are only taken by an explicit bind.
+    """
+    import random
+
+    rng = random.Random(os.getpid() ^ int.from_bytes(os.urandom(4), "little"))
+    for _ in range(200):
+        port = rng.randrange(20000, 32000)
+        with socket.socket() as s:
+            try:
+                s.bind(("127.0.0.1", port))
+            except OSError:
+                continue
+        return port
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
@@ -43,9 +60,17 @@ def _entry(rank, world, fn, port, out, args):
 
 
 def run(world: int, fn, *args) -> list[dict]:
-    port = free_port()
-    out = os.path.join(tempfile.gettempdir(), f"mtpb_mp_{os.getpid()}_{port}")
-    mp.start_processes(_entry, args=(world, fn, port, out, args), nprocs=world, join=True, start_method="spawn")
+    for attempt in range(3):
+        port = free_port()
+        out = os.path.join(tempfile.gettempdir(), f"mtpb_mp_{os.getpid()}_{port}")
+        try:
+            mp.start_processes(_entry, args=(world, fn, port, out, args), nprocs=world, join=True,
+                               start_method="spawn")
+            break
+        except mp.ProcessRaisedException as e:
+            # the store's port was taken between the choice and the bind: choose again
+            if "EADDRINUSE" not in str(e) or attempt == 2:
+                raise
     res = []
     for r in range(world):
         with np.load(f"{out}.{r}.npz") as f:

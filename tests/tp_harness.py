@@ -18,9 +18,10 @@ import torch.multiprocessing as mp
 
 
 def free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A rendezvous port below Linux's ephemeral range (see tests/mp_worker.py)."""
+    from tests.mp_worker import free_port as _free_port
+
+    return _free_port()
 
 
 def _worker(rank: int, world: int, fn, port: int, out_path: str, args: tuple, env: dict, init_pg: bool,
