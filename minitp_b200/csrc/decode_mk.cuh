@@ -970,6 +970,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
       if (k == 0 || k == 6) {
         if (k == 0) MK_TRACE(c, p, tb + 0);
         first_off = chunk_wait();
+        if (k == 6) MK_TRACE(c, p, tb + 3);  // the gate/up chunk (with ln2) has landed
         const T* gain = reinterpret_cast<const T*>(ring + first_off);
         if (k == 0) qkv_bias = ly.qkv_b ? reinterpret_cast<const T*>(ring + first_off + hvec) : nullptr;
         const int site = 2 * l + (k == 6 ? 1 : 0);
