@@ -376,8 +376,10 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, const char* rows
   // plain loads through pointers into the shared-memory array: the compiler
   // sees their address space and schedules them freely
   auto ld16 = [](const char* a) { return *reinterpret_cast<const uint4*>(a); };
-  // split K over warps only for long rows (more than 4 vectors per lane)
-  const int kp = n >= kMkCons ? 1 : max(1, min(kMkDivCons[n], (cpr + 127) >> 7));
+  // fewer units than warps: split K over the idle warps, at least one
+  // 16-byte vector per lane each (short stages such as O and QKV then use
+  // most warps instead of one warp per unit)
+  const int kp = n >= kMkCons ? 1 : max(1, min(kMkDivCons[n], (cpr + 31) >> 5));
   const int nw = n * kp;
   for (int w = c.cw; w < nw; w += kMkCons) {
     int j = w, q = 0;
