@@ -1,23 +1,35 @@
 """Decode throughput of the B200 TP path: ``python bench.py --gpus N --steps K --warmup W``.
 
 One step = one fixed-length greedy generation over a batch of synthetic
-prompts (Qwen2.5-0.5B shape by default: B=1, prompt 128, 128 new tokens,
-bf16, seeded random weights) at TP = N (one process per GPU under torchrun).
-The prefill runs eagerly; the 127 decode steps are replays of one CUDA graph
-of the device-resident decode step.
+prompts at TP = N (one process per GPU under torchrun): the Qwen2.5-0.5B
+shape (B=1, prompt 128, 128 new tokens) at N <= 2, the Qwen2.5-7B shape
+(prompt 1024, 256 new tokens, B = 1, 8 and 32) at N >= 4; bf16, seeded
+random weights. The prefill runs eagerly; the decode steps are replays of
+the CUDA graph of the device-resident decode step, captured once per shape
+during warm-up (the decode session ``generate_greedy`` keeps).
 
 Reported (rank 0, one JSON line):
 * value: decode tokens/s = B * decode steps / decode time, where the decode
-  time is measured with CUDA events per step and the max over ranks is taken.
+  time is measured with CUDA events per step and the max over ranks is taken
+  (the first batch of the run; the others under ``batches``).
 * e2e: the same metric through ``generate_greedy``, starting from pinned host
   prompt ids and ending with the output ids copied back to the host.
-* roofline: the dominant kernel (the LM-head GEMV streams the largest weight
-  of the token), timed live with CUDA events over repeated launches;
-  achieved = its weight bytes / launch time. roofline_token: (weight + KV)
-  bytes read per token per rank / measured time per token.
-* cpu_baseline: the CPU oracle port of the reference (rank 0, N=1 only) on
-  a bounded sample (prefill + 8 decode tokens).
-``--impl reference`` times that CPU port as the reference arm.
+* parity: before any timing, fp32 greedy generations of shapes whose
+  reference fixtures are committed (tests/golden), compared token for token
+  on every rank; a mismatch makes the run exit non-zero.
+* roofline: the decode step (one megakernel launch per token when the
+  library plans it): (weight + KV bytes read per token per rank) / time per
+  token vs the measured HBM peak; roofline_gemv: the prefill GEMV on the
+  LM-head weights; roofline_prefill_gemm: the tensor-core GEMM.
+* N > 1: fused_ar (fused AllReduce + residual + RMSNorm vs NCCL all_reduce,
+  next to the measured NVLink one-way latency) and embed_argmax (the masked
+  embedding and the distributed argmax vs the reference's torch + NCCL
+  formulation of the same operations).
+* cpu_baseline (N=1): the reference's CPU path restated per rank
+  (oracle/rank.py) on the host cores, on a bounded sample.
+``--impl reference`` times that CPU path as the reference arm: one Gloo
+process per rank with cores // N threads each (rank 0 of a torchrun launch
+spawns them; the other ranks exit at once).
 """
 
 from __future__ import annotations
@@ -25,7 +37,9 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
+import socket
 import statistics
 import subprocess
 import sys
@@ -38,8 +52,10 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 MEASURED_PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+GOLDEN = os.path.join(REPO, "tests", "golden")
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+NVLINK_GBS = 900.0  # nominal per direction per GPU
 
 
 def parse_args(argv=None):
@@ -48,17 +64,20 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    p.add_argument("--model", default="qwen2.5-0.5b", choices=["qwen2.5-0.5b", "qwen2.5-7b", "tiny"])
-    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--model", default=None, choices=["qwen2.5-0.5b", "qwen2.5-7b", "tiny"],
+                   help="default: qwen2.5-0.5b at N <= 2, qwen2.5-7b at N >= 4")
+    p.add_argument("--batch", type=int, default=None, help="one batch size (default: 1; 7B: 1, 8, 32)")
     p.add_argument("--prompt", type=int, default=None)
     p.add_argument("--new-tokens", type=int, default=None)
     p.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     p.add_argument("--gen-device", default=None, help="where synthetic weights are drawn (cpu|cuda)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true")
+    p.add_argument("--no-collectives", action="store_true", help="N > 1: skip the fused_ar / embed_argmax blocks")
     p.add_argument("--no-pdl", action="store_true")
     p.add_argument("--out", default=None, help="also write the JSON line here")
     p.add_argument("--workload", default="decode", choices=["decode", "fused_ar", "prefill_gemm"],
-                   help="decode (default), the fused AllReduce+residual+RMSNorm microbenchmark, or the "
+                   help="decode (default), the fused AllReduce+residual+RMSNorm microbenchmark alone, or the "
                         "tensor-core prefill GEMM sweep")
     p.add_argument("--gemm-shapes", default=None,
                    help="prefill_gemm: comma-separated names of the shapes to run (default: all)")
@@ -66,16 +85,20 @@ def parse_args(argv=None):
     return p.parse_args(argv)
 
 
-def workload(args):
+def workload(args, world: int):
+    """(model name, config, prompt length, new tokens, batch sizes)."""
     from minitp_b200 import config as mcfg
 
-    if args.model == "qwen2.5-7b":
-        cfg, prompt, new = mcfg.qwen25_7b(), 1024, 256
-    elif args.model == "tiny":
-        cfg, prompt, new = mcfg.baseline_tiny(), 8, 16
+    name = args.model or ("qwen2.5-0.5b" if world <= 2 else "qwen2.5-7b")
+    if name == "qwen2.5-7b":
+        cfg, prompt, new, batches = mcfg.qwen25_7b(), 1024, 256, [1, 8, 32]
+    elif name == "tiny":
+        cfg, prompt, new, batches = mcfg.baseline_tiny(), 8, 16, [1]
     else:
-        cfg, prompt, new = mcfg.qwen25_05b(), 128, 128
-    return cfg, args.prompt or prompt, args.new_tokens or new
+        cfg, prompt, new, batches = mcfg.qwen25_05b(), 128, 128, [1]
+    if args.batch:
+        batches = [args.batch]
+    return name, cfg, args.prompt or prompt, args.new_tokens or new, batches
 
 
 def peaks():
@@ -94,6 +117,24 @@ def peak_tflops():
             return float(json.load(f)["bf16_tflops"]), "measured (burst)"
     except Exception:
         return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def free_port() -> int:
+    """A rendezvous port below Linux's ephemeral range (32768+), so NCCL/Gloo sockets cannot take it."""
+    import random
+
+    rng = random.Random(os.getpid() ^ int.from_bytes(os.urandom(4), "little"))
+    for _ in range(200):
+        port = rng.randrange(20000, 32000)
+        with socket.socket() as s:
+            try:
+                s.bind(("127.0.0.1", port))
+            except OSError:
+                continue
+        return port
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def time_prefill_gemm(epi: str, M: int, N: int, K: int, dev, reps: int = 20) -> dict:
@@ -192,7 +233,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- #
-# bytes per token
+# bytes per token, launches
 # ---------------------------------------------------------------------- #
 def weight_bytes_per_token(model) -> int:
     """Weight bytes one decode step streams on this rank (all GEMV weights + LM head)."""
@@ -210,90 +251,485 @@ def kv_bytes_per_token(model, batch: int, avg_len: float) -> float:
     return per_pos * avg_len * batch * len(model.model.layers)
 
 
-# DRAM bytes (read + write) of one decode_mk_kernel launch from an ncu capture
-# (profiles/decode_mk_kernel_qwen05b_tp1_b1.md), keyed by (model, batch, TP).
-MK_TRAFFIC = {("qwen2.5-0.5b", 1, 1): 994_280_704}
+# DRAM bytes (read + write) of one decode-step launch measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (model, batch, TP,
+# kernel revision). Configurations without a capture of the current kernel
+# report null.
+MK_TRAFFIC: dict = {}
+MK_REVISION = 2
 
 
-def measured_traffic(args, world: int, step_launches: int):
+def measured_traffic(model_name: str, batch: int, world: int, step_launches: int):
     if step_launches != 1:
         return None
-    return MK_TRAFFIC.get((args.model, args.batch, world))
+    return MK_TRAFFIC.get((model_name, batch, world, MK_REVISION))
 
 
-def launches_per_generation(n_layers: int, new_tokens: int, prefill_tokens: int, step_launches: int) -> int:
-    """minitp_b200 kernel launches of one fixed-length generation.
+def decode_launches(model, batch: int, cap: int) -> int:
+    from minitp_b200 import _lib
 
-    Prefill runs the kernel chain; every decode step makes `step_launches`
-    launches (1 when the decode megakernel runs it, as the library reports).
+    nk = ctypes.c_int(0)
+    _lib.call("mtpb_model_decode_kernels", model.native(), batch, cap, ctypes.byref(nk))
+    return nk.value
+
+
+def prefill_launch_count(n_layers: int, chunks: int, consume_pass: bool) -> int:
+    """Kernel launches of a prefill through the kernel chain.
+
+    Per chunk: the embedding, 5 per layer (QKV, attention, O, gate/up, down)
+    and, when the chunk's rows do not fit the GEMV's shared-memory staging, a
+    separate AllReduce-consume pass in front of QKV and gate/up; then the
+    final norm's consume pass and the LM head of the last chunk.
     """
-    prefill = 1 + n_layers * 5 + (2 * n_layers + 1 if prefill_tokens > 1 else 0) + 1
-    select = 2  # argmax rows + finish
-    seed = 1  # decode position store
-    return prefill + select + seed + (new_tokens - 1) * step_launches
+    per_chunk = 1 + 5 * n_layers + (2 * n_layers if consume_pass else 0)
+    return chunks * per_chunk + (1 if consume_pass else 0) + 1
+
+
+def launches_per_generation(prefill: int, new_tokens: int, step_launches: int) -> int:
+    """Launches of one fixed-length generation: the prefill, the greedy pick of its
+    last position (argmax rows + finish), the decode position seed and the decode
+    steps (`step_launches` each: 1 when the decode megakernel runs them)."""
+    return prefill + 2 + 1 + (new_tokens - 1) * step_launches
+
+
+def prefill_launches(model, batch: int, prompt_len: int, comm) -> int:
+    """Prefill launches for this model and shape (chunked by the communicator slot)."""
+    cfg = model.cfg
+    esz = model.lm_head.weight.element_size()
+    row = batch * cfg.hidden_size * esz
+    tc = max(1, min(prompt_len, comm.slot_bytes() // row))
+    consume = batch * tc * cfg.hidden_size * esz > 64 * 1024  # GEMV x staging limit
+    return prefill_launch_count(cfg.num_hidden_layers, math.ceil(prompt_len / tc), consume)
 
 
 # ---------------------------------------------------------------------- #
-# CPU baseline (oracle port of the reference)
+# parity before timing
 # ---------------------------------------------------------------------- #
-_ORACLE_MODELS: dict = {}
+# name: (config factory, batch, prompt, new tokens); fp32 runs whose reference
+# ids are committed in tests/golden
+PARITY_MODELS = {
+    "q05b": ("qwen25_05b", None, 1, 128, 128),
+    "q05b_b4": ("qwen25_05b", None, 4, 32, 16),
+    "q7b_l2": ("qwen25_7b", 2, 1, 16, 8),
+}
+# world -> [(run, fixture)]: the reference's own TP=N run where one exists;
+# at TP=8 (and 0.5B at TP=4) the reference rejects the head count, so the
+# padded runs are held to the reference's TP=1 ids
+PARITY_RUNS = {
+    1: [("q05b", "model_q05b_tp1_fp32.npz")],
+    2: [("q05b", "model_q05b_tp2_fp32.npz"), ("q05b_b4", "model_q05b_b4_tp2_fp32.npz")],
+    4: [("q7b_l2", "model_q7b_l2_tp4_fp32.npz"), ("q05b_b4", "model_q05b_b4_tp1_fp32.npz")],
+    8: [("q7b_l2", "model_q7b_l2_tp1_fp32.npz"), ("q05b_b4", "model_q05b_b4_tp1_fp32.npz")],
+}
 
 
-def cpu_oracle_decode(cfg, batch, prompt_len, sample_tokens, dtype, tp, threads, passes=1):
-    """Decode tok/s of the oracle port on the host cores.
+def run_parity(ctx, world: int) -> list[dict]:
+    import numpy as np
+    import torch.distributed as dist
 
-    Each pass: fresh KV caches, prefill of the prompt (untimed), then
-    ``sample_tokens`` timed greedy decode steps. The model (synthetic weights)
-    is built once per shape and kept for later calls.
+    from minitp_b200 import config as mcfg
+    from minitp_b200.generation import generate_greedy
+    from minitp_b200.weight_loader import load_synthetic_tp
+
+    out = []
+    for run, fixture in PARITY_RUNS.get(world, []):
+        fac, layers, b, p, n = PARITY_MODELS[run]
+        cfg = getattr(mcfg, fac)(layers) if layers else getattr(mcfg, fac)()
+        model = load_synthetic_tp(cfg, ctx, dtype=torch.float32, device=ctx.device)
+        with np.load(os.path.join(GOLDEN, fixture)) as g:
+            prompt, want = torch.from_numpy(g["prompt"]), torch.from_numpy(g["tokens"])
+        got = generate_greedy(model, prompt.to(ctx.device), n, early_stop=False)
+        launches = decode_launches(model, b, p + n)
+        ctx.comm().raise_on_error()
+        equal = torch.tensor([int(torch.equal(got.cpu(), want))], device=ctx.device)
+        if world > 1:
+            allg = [torch.empty_like(got) for _ in range(world)]
+            dist.all_gather(allg, got.contiguous())
+            agree = all(torch.equal(x, allg[0]) for x in allg)
+            dist.all_reduce(equal, op=dist.ReduceOp.MIN)
+        else:
+            agree = True
+        out.append({"run": run, "fixture": fixture, "tp": world, "dtype": "fp32",
+                    "tokens_equal": bool(equal.item()), "ranks_agree": bool(agree),
+                    "new_tokens": n, "decode_launches": launches, "heads_padded": bool(model.cfg.is_padded)})
+        model.release_native()
+        del model, got
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------- #
+# decode timing
+# ---------------------------------------------------------------------- #
+def decode_bench(model, ctx, model_name, batch, prompt_len, new_tokens, args, flush, with_e2e):
+    """Device-timed decode (graph replays of the session's captured step), step time, e2e."""
+    import torch.distributed as dist
+
+    from minitp_b200.generation import GenerationState, decode_session, generate_greedy
+    from minitp_b200.synthetic import make_prompt
+
+    dev = ctx.device
+    world = ctx.tp_size
+    ids_host = make_prompt(model.cfg.vocab_size, batch, prompt_len).pin_memory()
+    ids = ids_host.to(dev)
+    sess = decode_session(model, batch, prompt_len + new_tokens, dev)
+
+    def one_step():
+        st = GenerationState(model, ids, new_tokens, session=sess)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        logits = st.prefill(last_only=True)
+        tok = st.select_next(logits)
+        st.append(tok)
+        st.start_device_decode(tok)
+        replays = new_tokens - 1
+        if st._graph is None:  # the first call of the shape: eager step, then capture (warm-up)
+            st.device_step()
+            st.capture()
+            replays -= 1
+        ev[1].record()
+        for _ in range(replays):
+            st.graph_step()
+        ev[2].record()
+        return st, ev, replays
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(1, args.warmup)):
+        st, _, _ = one_step()
+        st.release()
+        flush.zero_()
+    barrier()
+    ctx.comm().raise_on_error()
+
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
+    decode_ms, step_ms = [], []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()  # L2 flush between timed steps (256 MiB > 126 MB L2)
+        st, ev, replays = one_step()
+        torch.cuda.synchronize()
+        decode_ms.append(ev[1].elapsed_time(ev[2]) / max(1, replays))
+        step_ms.append(ev[0].elapsed_time(ev[2]))
+        st.release()
+    barrier()
+    clocks = sampler.stop()
+    ctx.comm().raise_on_error()
+    t = torch.tensor([statistics.mean(decode_ms), statistics.mean(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_token, ms_per_step = t.tolist()
+    res = {"batch": batch, "ms_per_token": ms_per_token, "ms_per_step": ms_per_step, "clocks": clocks,
+           "tok_s": batch / (ms_per_token / 1e3), "launches": decode_launches(model, batch, prompt_len + new_tokens),
+           "prefill_launches": prefill_launches(model, batch, prompt_len, ctx.comm())}
+    if with_e2e:
+        e2e_ms = []
+        e2e_warm = 1
+        for i in range(e2e_warm + max(2, min(args.steps, 5))):
+            flush.zero_()
+            barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = generate_greedy(model, ids_host.to(dev, non_blocking=True), new_tokens, early_stop=False)
+            out.to("cpu", non_blocking=False)
+            e.record()
+            torch.cuda.synchronize()
+            if i >= e2e_warm:
+                e2e_ms.append(s.elapsed_time(e))
+        te = torch.tensor([statistics.mean(e2e_ms)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        res["e2e"] = {"value": round(batch * new_tokens / (te.item() / 1e3), 2), "unit": "tok/s",
+                      "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
+                      "d2h_bytes_per_step": batch * (prompt_len + new_tokens) * 8,
+                      "definition": "generate_greedy from pinned host ids to host output ids, incl. prefill",
+                      "warmup": e2e_warm, "samples_ms": [round(x, 3) for x in e2e_ms]}
+    return res
+
+
+# ---------------------------------------------------------------------- #
+# collectives (N > 1)
+# ---------------------------------------------------------------------- #
+def _graph_time_us(fn, reps_total: int, chunk: int, dev) -> float:
+    """Device time per call of `fn`, replayed from a CUDA graph of `chunk` calls (max over ranks)."""
+    import torch.distributed as dist
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(chunk):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = max(1, reps_total // chunk)
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for _ in range(reps):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (reps * chunk)
+    del graph
+    t = torch.tensor([us], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def nvlink_floor(ctx, iters: int = 20000, warm: int = 1000) -> dict:
+    """One-way latency of one 8-byte LL word between ranks 0 and 1 (ping-pong, device-timed)."""
+    import torch.distributed as dist
+
+    from minitp_b200 import _lib
+
+    comm = ctx.comm()
+    ns = torch.zeros(1, dtype=torch.int64, device=ctx.device)
+    dist.barrier()
+    if ctx.tp_rank in (0, 1):
+        _lib.call("mtpb_comm_pingpong", comm.handle, 1 - ctx.tp_rank, iters, warm, ns.data_ptr(),
+                  _lib.stream_ptr(ctx.device))
+    torch.cuda.synchronize()
+    dist.all_reduce(ns, op=dist.ReduceOp.MAX)
+    comm.raise_on_error()
+    rt = ns.item() / (iters - warm) / 1e3
+    return {"one_way_us": round(rt / 2, 3), "round_trip_us": round(rt, 3), "iters": iters - warm,
+            "how": "one 8-byte LL word bounced between ranks 0 and 1 over NVLink, %globaltimer on the device"}
+
+
+def fused_ar_block(ctx, iters: int, floor_us: float | None) -> list[dict]:
+    """Fused AllReduce + residual + RMSNorm vs NCCL all_reduce, [rows, 896] bf16."""
+    import torch.distributed as dist
+
+    from minitp_b200 import _lib
+    from minitp_b200.synthetic_cases import fused_ar_case
+
+    comm = ctx.comm()
+    dev = ctx.device
+    world = ctx.tp_size
+    out = []
+    for rows in (1, 8, 64, 128, 512, 2048):
+        partials, residual, gain = fused_ar_case(rows, 896, world, seed=1000 + rows)
+        p = partials[ctx.tp_rank].to(dev)
+        r = residual.to(dev)
+        g = gain.to(dev)
+        out_res = torch.empty_like(p)
+        out_norm = torch.empty_like(p)
+        nccl_t = p.clone()
+
+        def fused():
+            _lib.call("mtpb_allreduce_residual_rmsnorm", comm.handle, p.data_ptr(), r.data_ptr(), g.data_ptr(),
+                      None, out_res.data_ptr(), out_norm.data_ptr(), rows, 896, 1e-6, _lib.MTPB_BF16,
+                      _lib.stream_ptr(dev))
+
+        def nccl():
+            dist.all_reduce(nccl_t)
+
+        f_us = _graph_time_us(fused, iters, 100, dev)
+        n_us = _graph_time_us(nccl, iters, 100, dev)
+        comm.raise_on_error()
+        m = rows * 896 * 2
+        line = {"rows": rows, "bytes": m, "fused_us": round(f_us, 3), "nccl_allreduce_us": round(n_us, 3),
+                "ratio_fused_over_nccl": round(f_us / n_us, 3),
+                "fused_send_gbs": round((world - 1) * m / (f_us * 1e-6) / 1e9, 2),
+                "fused_send_frac_of_900": round((world - 1) * m / (f_us * 1e-6) / 1e9 / NVLINK_GBS, 4),
+                "iters": max(1, iters // 100) * 100}
+        if floor_us:
+            line["fused_over_floor"] = round(f_us / floor_us, 2)
+        out.append(line)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return out
+
+
+def embed_argmax_block(ctx, iters: int = 2000) -> list[dict]:
+    """Vocab-parallel embedding + distributed argmax vs the reference's formulation.
+
+    Ours: ops.embedding (masked local lookup + NVLink reduce in one kernel) and
+    ops.argmax (packed-key argmax over the shard + O(tp) NVLink gather). The
+    reference's (minitp/parallel/embedding.py:44-50, 118-172): F.embedding of
+    the masked ids, a mask multiply and an NCCL all_reduce; NaN cleanup, a
+    local max, the bitpack key and an NCCL all_gather_into_tensor. Both run
+    from CUDA graphs on the same box; ids and embeddings are compared.
     """
-    from oracle.model import OracleConfig, OracleModel, checkpoint_tensors, prompt
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from minitp_b200 import ops
+    from minitp_b200.parallel.linear import shard_range
+    from minitp_b200.synthetic_cases import argmax_logits
+
+    comm = ctx.comm()
+    dev = ctx.device
+    world, rank = ctx.tp_size, ctx.tp_rank
+    hbm, _ = peaks()
+    out = []
+    for vocab in (151936, 151937):
+        s, e = shard_range(vocab, rank, world)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(vocab)
+        table = (torch.randn(e - s, 896, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        for batch in (1, 8, 64):
+            g = torch.Generator().manual_seed(vocab * 7 + batch)
+            ids = torch.randint(0, vocab, (batch, 1), generator=g).to(dev)
+            logits = argmax_logits(vocab, batch, seed=vocab + batch)[:, s:e].contiguous().to(dev)
+            gather_buf = torch.empty(world, batch, dtype=torch.int64, device=dev)
+
+            def ref_embed():
+                mask = (ids >= s) & (ids < e)
+                x = F.embedding((ids - s) * mask, table) * mask.unsqueeze(-1).to(table.dtype)
+                dist.all_reduce(x)
+                return x
+
+            def ref_argmax():
+                clean = torch.where(torch.isnan(logits), torch.full_like(logits, float("-inf")), logits)
+                values, idx = clean.max(dim=-1)
+                gid = idx + s
+                vals = torch.where(values == 0, torch.zeros_like(values), values)
+                bits = vals.float().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+                key = torch.where(bits < 0x80000000, bits, ((~bits) & 0xFFFFFFFF) - 0x80000000)
+                packed = (key << 32) | (0xFFFFFFFF - gid.to(torch.int64))
+                dist.all_gather_into_tensor(gather_buf, packed)
+                winner = gather_buf.max(dim=0).values
+                return 0xFFFFFFFF - (winner & 0xFFFFFFFF)
+
+            mine_e = ops.embedding(ids, table, s, e, vocab, comm)
+            mine_a = ops.argmax(logits, s, comm).view(-1)
+            ref_e, ref_a = ref_embed(), ref_argmax()
+            torch.cuda.synchronize()
+            t = {
+                "embed_us": _graph_time_us(lambda: ops.embedding(ids, table, s, e, vocab, comm), iters, 50, dev),
+                "ref_embed_us": _graph_time_us(ref_embed, iters, 50, dev),
+                "argmax_us": _graph_time_us(lambda: ops.argmax(logits, s, comm), iters, 50, dev),
+                "ref_argmax_us": _graph_time_us(ref_argmax, iters, 50, dev),
+            }
+            comm.raise_on_error()
+            read = batch * (e - s) * 4
+            out.append({"vocab": vocab, "batch": batch, **{k: round(v, 3) for k, v in t.items()},
+                        "embed_equal": bool(torch.equal(mine_e, ref_e)), "ids_equal": bool(torch.equal(mine_a, ref_a)),
+                        "argmax_read_bytes": read, "argmax_hbm_gbs": round(read / (t["argmax_us"] * 1e-6) / 1e9, 1),
+                        "argmax_frac_of_hbm": round(read / (t["argmax_us"] * 1e-6) / 1e9 / hbm, 4)})
+    torch.cuda.synchronize()
+    dist.barrier()
+    return out
+
+
+# ---------------------------------------------------------------------- #
+# the reference's CPU path (Gloo ranks)
+# ---------------------------------------------------------------------- #
+def _ref_worker(rank, world, port, out_path, cfg_kw, dtype_name, batch, prompt_len, sample, fill_cache, threads,
+                warmup, steps):
+    import torch.distributed as dist
+
+    from oracle.model import OracleConfig
+    from oracle.rank import OracleRank
 
     torch.set_num_threads(threads)
-    key = (repr(cfg), str(dtype), tp)
-    model = _ORACLE_MODELS.get(key)
-    if model is None:
-        model = OracleModel(OracleConfig.of(cfg), checkpoint_tensors(cfg), tp=tp, dtype=dtype)
-        _ORACLE_MODELS.clear()
-        _ORACLE_MODELS[key] = model
-    ids = prompt(cfg.vocab_size, batch, prompt_len)
-    dt = 0.0
-    for _ in range(passes):
-        model.reset(batch, prompt_len + sample_tokens + 1)
-        logits = model.forward(ids, torch.arange(prompt_len))
-        tok = model.select(logits[:, -1])
+    if world > 1:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        cfg = OracleConfig(**cfg_kw)
+        dt = torch.bfloat16 if dtype_name == "bf16" else torch.float32
         t0 = time.perf_counter()
-        for i in range(sample_tokens):
-            logits = model.forward(tok[:, None], torch.tensor([prompt_len + i]))
-            tok = model.select(logits[:, -1])
-        dt += time.perf_counter() - t0
-    return batch * sample_tokens * passes / dt, dt
+        m = OracleRank(cfg, rank, world, dtype=dt, weights="fill")
+        build_s = time.perf_counter() - t0
+        g = torch.Generator().manual_seed(0)
+        ids = torch.randint(0, cfg.vocab_size, (batch, prompt_len), generator=g)
+        times = []
+        for i in range(warmup + steps):
+            if fill_cache:
+                m.reset(batch, prompt_len + sample + 1, fill_len=prompt_len)
+                tok = ids[:, -1]
+            else:
+                m.reset(batch, prompt_len + sample + 1)
+                tok = m.select(m.forward(ids)[:, -1])
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(sample):
+                tok = m.select(m.forward(tok[:, None])[:, -1])
+            dt_s = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt_s)
+        torch.save({"times": times, "build_s": build_s}, f"{out_path}.{rank}")
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
 
 
-def run_reference(args, cfg, prompt_len, new_tokens):
+def cpu_reference(cfg, world: int, dtype_name: str, batch: int, prompt_len: int, sample: int, fill_cache: bool,
+                  warmup: int, steps: int) -> dict:
+    """Decode tok/s of the reference's CPU path: `world` Gloo processes, cores // world threads each."""
+    import torch.multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // world)
+    cfg_kw = {k: getattr(cfg, k) for k in (
+        "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+        "head_dim", "vocab_size", "rms_norm_eps", "rope_theta", "max_position_embeddings", "tie_word_embeddings")}
+    port = free_port()
+    out_path = os.path.join(tempfile.gettempdir(), f"mtpb_ref_{os.getpid()}_{port}")
+    if world > 1:
+        mp.start_processes(_ref_worker, args=(world, port, out_path, cfg_kw, dtype_name, batch, prompt_len, sample,
+                                              fill_cache, threads, warmup, steps),
+                           nprocs=world, join=True, start_method="spawn")
+    else:
+        _ref_worker(0, 1, port, out_path, cfg_kw, dtype_name, batch, prompt_len, sample, fill_cache, threads,
+                    warmup, steps)
+    res = []
+    for r in range(world):
+        res.append(torch.load(f"{out_path}.{r}", weights_only=False))
+        os.remove(f"{out_path}.{r}")
+    per_step = [max(x["times"][i] for x in res) for i in range(steps)]  # max over ranks
+    value = batch * sample / statistics.median(per_step)
+    how = (f"KV cache pre-filled to {prompt_len} positions (no CPU prefill)" if fill_cache
+           else f"prefill of {prompt_len} untimed")
+    return {"value": value, "cores": threads * world, "threads_per_rank": threads, "ranks": world,
+            "sample": f"per step: {how}, then {sample} timed greedy decode steps of batch {batch}; "
+                      f"{world} Gloo process(es) x {threads} threads; max over ranks; median of {steps} steps",
+            "timed_s": round(sum(per_step), 2)}
+
+
+def reference_sample(cfg, prompt_len: int, new_tokens: int) -> tuple[int, bool]:
+    """(decode steps per sample, pre-fill the KV cache instead of a CPU prefill)."""
+    params = cfg.num_hidden_layers * cfg.hidden_size * (4 * cfg.hidden_size + 3 * cfg.intermediate_size)
+    if params > 2e9:  # 7B: a CPU prefill of the prompt would take minutes
+        return 3, True
+    return min(32, max(1, new_tokens - 1)), False
+
+
+def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return  # rank 0 runs the Gloo ranks itself
+    world = args.gpus
+    name, cfg, prompt_len, new_tokens, batches = workload(args, world)
+    batch = batches[0]
+    if cfg.num_attention_heads % world:
+        # minitp/config.py:50-61 (ModelConfig.validate)
+        msg = f"ValueError: num_attention_heads={cfg.num_attention_heads} not divisible by tp_size={world}"
+        print(json.dumps({"impl": "reference", "unavailable": f"the reference rejects {name} at TP={world}: {msg}",
+                          "n_gpus": world}), flush=True)
         return
-    threads = os.cpu_count() or 1
-    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    sample = max(1, new_tokens - 1)  # every decode step of one generation
-    vals = []
-    for _ in range(max(args.warmup, 0)):
-        cpu_oracle_decode(cfg, args.batch, prompt_len, 2, dtype, args.gpus, threads)
-    for _ in range(args.steps):
-        v, _ = cpu_oracle_decode(cfg, args.batch, prompt_len, sample, dtype, args.gpus, threads)
-        vals.append(v)
-    value = statistics.median(vals)
+    sample, fill = reference_sample(cfg, prompt_len, new_tokens)
+    r = cpu_reference(cfg, world, args.dtype, batch, prompt_len, sample, fill, max(1, args.warmup), args.steps)
+    value = r["value"]
     line = {
         "impl": "reference", "metric": "decode tok/s", "value": round(value, 3), "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * args.batch / value, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded random weights and prompts)",
-        "config": {"workload": f"{args.model} B={args.batch} P={prompt_len} new={new_tokens} tp={args.gpus}",
-                   "model": args.model, "global_batch": args.batch, "seq_len": prompt_len + new_tokens,
-                   "parallelism": f"tp{args.gpus} (emulated in one process)"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"per step: prefill {prompt_len} (untimed) + {sample} decode steps, oracle port "
-                                   f"of the reference CPU path, tp={args.gpus} emulated"},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * batch * sample / value, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (random weights, uniform prompt ids)",
+        "config": {"workload": f"{name} decode, B={batch}, prompt {prompt_len}, {new_tokens} new tokens, TP={world}",
+                   "model": name, "global_batch": batch, "seq_len": prompt_len + new_tokens,
+                   "parallelism": f"tp{world} (Gloo CPU ranks)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": r["cores"], "kind": "port",
+                         "sample": r["sample"] + "; oracle/rank.py restates the reference's per-rank CPU path"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -302,112 +738,45 @@ def run_reference(args, cfg, prompt_len, new_tokens):
 # ---------------------------------------------------------------------- #
 # B200 arm
 # ---------------------------------------------------------------------- #
-def run_b200(args, cfg, prompt_len, new_tokens):
+def run_b200(args):
     import torch.distributed as dist
 
     from minitp_b200 import _lib, ops
     from minitp_b200.build import build
     from minitp_b200.distributed.context import init_context
-    from minitp_b200.generation import GenerationState, generate_greedy
-    from minitp_b200.synthetic import make_prompt
     from minitp_b200.weight_loader import load_synthetic_tp
 
     if int(os.environ.get("RANK", "0")) == 0:
         build()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1:
-        # rank 0 built the library; the others wait for it through the store
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     ctx = init_context(timeout_s=120.0)
     if world > 1:
-        dist.barrier()
+        dist.barrier()  # rank 0 built the library before anyone loads it
     lib = _lib.load()
     if args.no_pdl:
         lib.mtpb_set_pdl(0)
     dev = ctx.device
+    name, cfg, prompt_len, new_tokens, batches = workload(args, world)
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    gen_dev = args.gen_device or ("cuda" if args.model == "qwen2.5-7b" else "cpu")
+
+    parity = [] if args.no_parity else run_parity(ctx, world)
+    parity_ok = all(x["tokens_equal"] and x["ranks_agree"] for x in parity)
+
+    gen_dev = args.gen_device or ("cuda" if name == "qwen2.5-7b" else "cpu")
     model = load_synthetic_tp(cfg, ctx, dtype=dtype, device=dev, seed=0, gen_device=gen_dev)
-    ids_host = make_prompt(cfg.vocab_size, args.batch, prompt_len).pin_memory()
-    ids = ids_host.to(dev)
-    comm = ctx.comm()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-
-    def one_step(timed: bool):
-        st = GenerationState(model, ids, new_tokens)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        ev[0].record()
-        logits = st.prefill(last_only=True)
-        tok = st.select_next(logits)
-        st.append(tok)
-        st.start_device_decode(tok)
-        st.device_step()
-        st.capture()
-        ev[1].record()
-        for _ in range(new_tokens - 2):
-            st.graph_step()
-        ev[2].record()
-        return st, ev
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        one_step(False)
-        flush.zero_()
-    barrier()
-    comm.raise_on_error()
-
-    sampler = ClockSampler(dev.index if dev.index is not None else 0)
-    sampler.start()
-    decode_ms, step_ms = [], []
-    barrier()
-    for _ in range(args.steps):
-        flush.zero_()  # L2 flush between timed steps (256 MiB > 126 MB L2)
-        st, ev = one_step(True)
-        torch.cuda.synchronize()
-        decode_ms.append(ev[1].elapsed_time(ev[2]) / max(1, new_tokens - 2))
-        step_ms.append(ev[0].elapsed_time(ev[2]))
-        st.release()
-    barrier()
-    clocks = sampler.stop()
-    comm.raise_on_error()
-
-    # max over ranks
-    t = torch.tensor([statistics.mean(decode_ms), statistics.mean(step_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_per_token, ms_per_step = t.tolist()
-    value = args.batch / (ms_per_token / 1e3)
-
-    # e2e through the public API: pinned host ids in, host ids out
-    e2e_ms = []
-    e2e_warm = 2
-    for i in range(e2e_warm + max(2, min(args.steps, 5))):
-        flush.zero_()
-        barrier()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        out = generate_greedy(model, ids_host.to(dev, non_blocking=True), new_tokens, early_stop=False)
-        host = out.to("cpu", non_blocking=False)
-        e.record()
-        torch.cuda.synchronize()
-        if i >= e2e_warm:  # the first calls are untimed warm-up, as for the device-timed steps
-            e2e_ms.append(s.elapsed_time(e))
-    te = torch.tensor([statistics.mean(e2e_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = args.batch * new_tokens / (te.item() / 1e3)
-
-    # decode launches per step as the library plans them (1 = megakernel)
-    nk = ctypes.c_int(0)
-    _lib.call("mtpb_model_decode_kernels", model.native(), args.batch, prompt_len + new_tokens, ctypes.byref(nk))
-    step_launches = nk.value
+    runs = []
+    for i, b in enumerate(batches):
+        runs.append(decode_bench(model, ctx, name, b, prompt_len, new_tokens, args, flush, with_e2e=(i == 0)))
+    main = runs[0]
+    batch = main["batch"]
+    ms_per_token = main["ms_per_token"]
+    step_launches = main["launches"]
 
     # the prefill GEMV, timed live: the LM-head weights over this rank's vocab shard
-    x = torch.randn(args.batch, cfg.hidden_size, device=dev).to(dtype)
+    x = torch.randn(batch, cfg.hidden_size, device=dev).to(dtype)
     w = model.lm_head.weight
     for _ in range(3):
         ops.linear(x, w)
@@ -422,64 +791,79 @@ def run_b200(args, cfg, prompt_len, new_tokens):
     torch.cuda.synchronize()
     k_ms = ks.elapsed_time(ke) / reps
     peak, peak_kind = peaks()
-    k_bytes = w.numel() * w.element_size() + x.numel() * x.element_size() + args.batch * w.shape[0] * w.element_size()
+    k_bytes = w.numel() * w.element_size() + x.numel() * x.element_size() + batch * w.shape[0] * w.element_size()
     k_gbs = k_bytes / (k_ms / 1e3) / 1e9
 
-    # the prefill GEMM (tensor cores) at this workload's prefill rows, gate/up shape
     gu = model.model.layers[0].mlp.gate_up_proj.weight
     tc_line = None
-    if dtype == torch.bfloat16 and args.batch * prompt_len >= 64:
-        tc_line = time_prefill_gemm("swiglu", args.batch * prompt_len, gu.shape[0], gu.shape[1], dev)
+    if dtype == torch.bfloat16 and batch * prompt_len >= 64:
+        tc_line = time_prefill_gemm("swiglu", batch * prompt_len, gu.shape[0], gu.shape[1], dev)
 
     wb = weight_bytes_per_token(model)
-    kvb = kv_bytes_per_token(model, args.batch, prompt_len + new_tokens / 2)
+    kvb = kv_bytes_per_token(model, batch, prompt_len + new_tokens / 2)
     tok_gbs = (wb + kvb) / (ms_per_token / 1e3) / 1e9
+
+    coll = {}
+    if world > 1 and not args.no_collectives:
+        floor = nvlink_floor(ctx)
+        coll["nvlink_floor"] = floor
+        coll["fused_ar"] = fused_ar_block(ctx, args.iters, floor["one_way_us"])
+        coll["embed_argmax"] = embed_argmax_block(ctx)
 
     line = None
     if ctx.is_rank_zero:
         line = {
-            "metric": "decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "metric": "decode tok/s", "value": round(main["tok_s"], 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms_per_step"], 4),
             "us_per_token": round(ms_per_token * 1e3, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.dtype,
             "data": "synthetic (seeded random weights N(0,0.02) and uniform prompt ids)",
             "config": {
-                "workload": f"{args.model} decode, B={args.batch}, prompt {prompt_len}, {new_tokens} new tokens, "
-                            f"TP={world}",
-                "model": args.model, "global_batch": args.batch, "seq_len": prompt_len + new_tokens,
+                "workload": f"{name} decode, B={batch}, prompt {prompt_len}, {new_tokens} new tokens, TP={world}",
+                "model": name, "global_batch": batch, "seq_len": prompt_len + new_tokens,
                 "parallelism": f"tp{world}", "heads_padded": bool(model.cfg.is_padded),
                 "l2": "flushed between timed steps (256 MiB write)",
-                "decode": "CUDA graph replay of the device-resident decode step (persistent megakernel)",
+                "decode": ("CUDA graph replay of the device-resident decode step (persistent megakernel)"
+                           if step_launches == 1 else f"CUDA graph replay of the kernel chain ({step_launches} "
+                                                      "launches per step)"),
+                "step": "prefill (eager) + greedy selection + decode graph replays; graph captured in warm-up",
             },
-            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
-                    "d2h_bytes_per_step": args.batch * (prompt_len + new_tokens) * 8,
-                    "definition": "generate_greedy from pinned host ids to host output ids, incl. prefill",
-                    "warmup": e2e_warm, "samples_ms": [round(x, 3) for x in e2e_ms]},
+            "e2e": main["e2e"],
+            "parity": parity,
             "roofline": {"bound": "hbm",
                          "kernel": "decode_mk_kernel" if step_launches == 1 else "decode kernel chain",
                          "achieved": round(tok_gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(tok_gbs / peak, 4), "traffic": measured_traffic(args, world, step_launches),
+                         "frac": round(tok_gbs / peak, 4),
+                         "traffic": measured_traffic(name, batch, world, step_launches),
                          "peak_kind": peak_kind,
                          "bytes_per_launch": round(wb + kvb), "weight_bytes": wb, "kv_bytes": round(kvb),
                          "us_per_launch": round(ms_per_token * 1e3, 3),
-                         "timing": "CUDA events over the graph replays of the decode step (one launch each)"},
+                         "timing": "CUDA events over the graph replays of the decode step"},
             "roofline_gemv": {"bound": "hbm", "kernel": "gemv_kernel (LM-head weights, prefill GEMV)",
                               "achieved": round(k_gbs, 1), "peak": peak, "unit": "GB/s",
                               "frac": round(k_gbs / peak, 4), "bytes_per_launch": k_bytes,
                               "us_per_launch": round(k_ms * 1e3, 3)},
             "roofline_prefill_gemm": tc_line,
-            "gpu_launches": launches_per_generation(cfg.num_hidden_layers, new_tokens, prompt_len,
-                                                    step_launches) * args.steps,
-            "clocks": clocks,
+            "gpu_launches": launches_per_generation(main["prefill_launches"], new_tokens, step_launches) * args.steps,
+            "clocks": main["clocks"],
         }
+        if len(runs) > 1:
+            line["batches"] = []
+            for r in runs:
+                kv_r = kv_bytes_per_token(model, r["batch"], prompt_len + new_tokens / 2)
+                gbs = (wb + kv_r) / (r["ms_per_token"] / 1e3) / 1e9
+                line["batches"].append({
+                    "batch": r["batch"], "tok_s": round(r["tok_s"], 2), "us_per_token": round(r["ms_per_token"] * 1e3, 3),
+                    "ms_per_step": round(r["ms_per_step"], 3), "decode_launches_per_token": r["launches"],
+                    "decode_path": "megakernel" if r["launches"] == 1 else "kernel chain",
+                    "roofline_frac": round(gbs / peak, 4), "bytes_per_token": round(wb + kv_r), "clocks": r["clocks"]})
+        line.update(coll)
         if world == 1 and not args.no_cpu_baseline:
-            threads = os.cpu_count() or 1
-            ns = max(1, new_tokens - 1)
-            v, dt = cpu_oracle_decode(cfg, args.batch, prompt_len, ns, dtype, 1, threads, passes=3)
-            line["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                                    "sample": f"3 x (prefill {prompt_len} untimed + {ns} decode steps), "
-                                              f"{dt:.1f} s timed, oracle port of the reference CPU path"}
+            sample, fill = reference_sample(cfg, prompt_len, new_tokens)
+            r = cpu_reference(cfg, 1, args.dtype, batch, prompt_len, sample, fill, 1, 3)
+            line["cpu_baseline"] = {"value": round(r["value"], 3), "unit": "tok/s", "cores": r["cores"],
+                                    "kind": "port", "sample": r["sample"] + "; oracle/rank.py (the reference's "
+                                                                            "per-rank CPU path restated)"}
     if world > 1:
         dist.barrier()
     model.release_native()
@@ -490,91 +874,31 @@ def run_b200(args, cfg, prompt_len, new_tokens):
             with open(args.out, "w") as f:
                 f.write(s + "\n")
     ctx.destroy()
+    if not parity_ok:
+        print("parity: a fixture's greedy ids were not reproduced", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 def run_fused_ar(args):
-    """Fused AllReduce + residual + RMSNorm vs NCCL all_reduce, [rows, 896] bf16.
-
-    Both are replayed from CUDA graphs of `chunk` back-to-back calls, so the
-    numbers are device time per call (max over ranks), not host launch time.
-    Prints one JSON line per size on rank 0.
-    """
+    """The fused AllReduce microbenchmark alone: one JSON line per size on rank 0."""
     import torch.distributed as dist
 
-    from minitp_b200 import ops
     from minitp_b200.build import build
     from minitp_b200.distributed.context import init_context
-    from minitp_b200.synthetic_cases import fused_ar_case
 
     if int(os.environ.get("RANK", "0")) == 0:
         build()
     ctx = init_context(timeout_s=120.0)
-    world = ctx.tp_size
-    if world < 2:
+    if ctx.tp_size < 2:
         if ctx.is_rank_zero:
             print(json.dumps({"workload": "fused_ar", "skipped": "needs >= 2 GPUs"}))
         return
     dist.barrier()
-    comm = ctx.comm()
-    dev = ctx.device
-    results = []
-    chunk = 100
-    for rows in (1, 8, 64, 128, 512, 2048):
-        partials, residual, gain = fused_ar_case(rows, 896, world, seed=1000 + rows)
-        p = partials[ctx.tp_rank].to(dev)
-        r = residual.to(dev)
-        g = gain.to(dev)
-        out_res = torch.empty_like(p)
-        out_norm = torch.empty_like(p)
-        nccl_t = p.clone()
-        from minitp_b200 import _lib
-
-        def fused():
-            _lib.call("mtpb_allreduce_residual_rmsnorm", comm.handle, p.data_ptr(), r.data_ptr(), g.data_ptr(),
-                      None, out_res.data_ptr(), out_norm.data_ptr(), rows, 896, 1e-6, _lib.MTPB_BF16,
-                      _lib.stream_ptr(dev))
-
-        def nccl():
-            dist.all_reduce(nccl_t)
-
-        times = {}
-        for name, fn in (("fused", fused), ("nccl", nccl)):
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            dist.barrier()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for _ in range(chunk):
-                    fn()
-            graph.replay()
-            torch.cuda.synchronize()
-            dist.barrier()
-            reps = max(1, args.iters // chunk)
-            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
-            s.record()
-            for _ in range(reps):
-                graph.replay()
-            e.record()
-            torch.cuda.synchronize()
-            us = s.elapsed_time(e) * 1e3 / (reps * chunk)
-            t = torch.tensor([us], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            times[name] = t.item()
-            del graph
-        comm.raise_on_error()
-        m = rows * 896 * 2
-        line = {"workload": "fused_ar", "metric": "fused AR+residual+RMSNorm latency", "rows": rows,
-                "bytes": m, "tp": world, "unit": "us", "fused_us": round(times["fused"], 3),
-                "nccl_allreduce_us": round(times["nccl"], 3),
-                "ratio_fused_over_nccl": round(times["fused"] / times["nccl"], 3),
-                "fused_nvlink_send_gbs": round((world - 1) * m / (times["fused"] * 1e-6) / 1e9, 2),
-                "iters": (max(1, args.iters // chunk)) * chunk}
-        results.append(line)
+    floor = nvlink_floor(ctx)
+    for line in fused_ar_block(ctx, args.iters, floor["one_way_us"]):
         if ctx.is_rank_zero:
-            print(json.dumps(line), flush=True)
-    torch.cuda.synchronize()
-    dist.barrier()
+            print(json.dumps({"workload": "fused_ar", "tp": ctx.tp_size, "nvlink_one_way_us": floor["one_way_us"],
+                              **line}), flush=True)
     ctx.destroy()
 
 
@@ -619,11 +943,10 @@ def main(argv=None):
     if args.workload == "prefill_gemm":
         run_prefill_gemm(args)
         return
-    cfg, prompt_len, new_tokens = workload(args)
     if args.impl == "reference":
-        run_reference(args, cfg, prompt_len, new_tokens)
+        run_reference(args)
     else:
-        run_b200(args, cfg, prompt_len, new_tokens)
+        run_b200(args)
 
 
 if __name__ == "__main__":

@@ -81,6 +81,14 @@ int* mtpb_comm_pos_ptr(void* comm);
 /* Enqueue a store of `pos` into that decode position (a one-thread kernel). */
 int mtpb_comm_set_pos(void* comm, int pos, void* stream);
 uint64_t mtpb_comm_slot_bytes(void* comm);
+/* NVLink latency floor (measurement only; no counterpart in the reference):
+ * this rank and `peer` bounce one 8-byte word `iters` times (both ranks make
+ * the call, in the same order of calls); *ns_out (device memory) receives the
+ * time of the last iters - warm round trips. One-way latency =
+ * ns / (iters - warm) / 2. Waits are bounded by the communicator timeout
+ * (status bit 1 on expiry). */
+int mtpb_comm_pingpong(void* comm, int peer, int iters, int warm, unsigned long long* ns_out,
+                       void* stream);
 
 /* --------------------------------------------------------------- linear
  * y[M, N] = x[M, K] * w[N, K]^T (+ bias[N]), x rows `ldx` elements apart,
@@ -136,11 +144,18 @@ int mtpb_attention(const void* q, const void* k_cache, const void* v_cache, void
  * device current; make that first call before any stream capture. All calls
  * on a device share the one array: calls that overlap on the GPU (on
  * different streams, or from several threads) race and must be ordered by
- * the caller. Each call clears the counters it needs at its start. */
+ * the caller. Each call clears the counters it needs at its start.
+ *
+ * `status` (device memory of the caller, may be NULL): a 32-bit word into
+ * which the kernel ORs its error bits (the bits mtpb_comm_status reports:
+ * 1 timeout, 2 bad position, 4 bad token). The caller reads it, and
+ * clears it, whenever it chooses. With NULL the bits land in a word of the
+ * fixed array that no call reads back, so device-side errors are then not
+ * reported (the host checks above reject every input that sets one today). */
 #define MTPB_NOALLOC_SCRATCH_BYTES (4u << 20)
 int mtpb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
                            int T, int hq, int hkv, int hd, int cap, int cache_len, int dtype,
-                           void* stream);
+                           uint32_t* status, void* stream);
 
 /* RMSNorm: y = T(x * rsqrt(mean(x^2) + eps) * w) in fp32 math.
  * ref: minitp/layer.py:36-42. */

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_comm_pos_ptr": (c_void_p, [c_void_p]),
     "mtpb_comm_set_pos": (c_int, [c_void_p, c_int, c_void_p]),
     "mtpb_comm_slot_bytes": (c_uint64, [c_void_p]),
+    "mtpb_comm_pingpong": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "mtpb_linear": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                             c_void_p]),
     "mtpb_linear_swiglu": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
@@ -87,7 +88,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_void_p, c_void_p]),
     "mtpb_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                                       c_int, c_int, c_int, c_void_p]),
+                                       c_int, c_int, c_int, c_void_p, c_void_p]),
     "mtpb_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_void_p]),
     "mtpb_allreduce": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "mtpb_allreduce_residual_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

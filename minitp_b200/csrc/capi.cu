@@ -85,6 +85,7 @@ struct CommHost {
   void* mapped[kMaxRanks] = {};
   int device = 0;
   bool open = false;
+  uint32_t ping_calls = 0;  // mtpb_comm_pingpong calls (their sequence numbers)
 };
 
 // A communicator-less call still needs control words and a local slot: a
@@ -1207,6 +1208,28 @@ int mtpb_comm_set_pos(void* comm, int pos, void* stream) {
   return launch(set_i32_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream), SetI32{p, pos});
 }
 
+int mtpb_comm_pingpong(void* comm, int peer, int iters, int warm, unsigned long long* ns_out, void* stream) {
+  CommHost* c = as_comm(comm);
+  if (!c || !c->open) return fail(MTPB_ERR_INVALID, "pingpong: communicator not open");
+  if (peer < 0 || peer >= c->dev.world || peer == c->dev.rank)
+    return fail(MTPB_ERR_INVALID, "pingpong: peer must be another rank of the communicator");
+  if (iters <= 0 || warm < 0 || warm >= iters || iters > (1 << 20))
+    return fail(MTPB_ERR_INVALID, "pingpong: need 0 <= warm < iters <= 2^20");
+  if (!ns_out) return fail(MTPB_ERR_INVALID, "pingpong: null output");
+  PingParams p;
+  p.comm = c->dev;
+  p.peer = peer;
+  p.iters = iters;
+  p.warm = warm;
+  // both ranks count their calls alike, so they agree on the base; 2^31 and
+  // above, with room for 2^20 round trips per call
+  p.base = 0x80000000u + (c->ping_calls++ % 1024u) * (2u << 20);
+  p.ns_out = ns_out;
+  pingpong_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  MTPB_CUDA(cudaGetLastError());
+  return MTPB_OK;
+}
+
 uint64_t mtpb_comm_slot_bytes(void* comm) {
   CommHost* c = as_comm(comm);
   return c ? c->dev.slot_bytes : 0;
@@ -1568,7 +1591,7 @@ int mtpb_model_decode_step(void* model, int64_t* tok, int B, void* const* k_cach
 // array instead of memory the library allocates. The array is part of the
 // module image: every GPU that loads the library holds it until the process
 // exits. Layout of one call (offsets rounded up to 256 bytes):
-//   [0, 256)              status word of the kernel (never read back)
+//   [0, 256)              status word of the kernel when the caller passes none
 //   counters u32[M*hkv]   last-CTA merge counters, cleared by every call
 //   part_ml  f32[M*hq*splits*2], part_o f32[M*hq*splits*hd]
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[MTPB_NOALLOC_SCRATCH_BYTES];
@@ -1599,7 +1622,7 @@ int noalloc_scratch_addr(char** out) {
 
 extern "C" int mtpb_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
                                       int T, int hq, int hkv, int hd, int cap, int cache_len, int dtype,
-                                      void* stream) {
+                                      uint32_t* status, void* stream) {
   if (!q || !k_cache || !v_cache || !out) return fail(MTPB_ERR_INVALID, "attention_noalloc: null tensor");
   if (B <= 0 || T <= 0 || hq <= 0 || hkv <= 0 || hd <= 0 || cap <= 0 || cache_len < 0)
     return fail(MTPB_ERR_INVALID, "attention_noalloc: sizes must be positive");
@@ -1629,6 +1652,8 @@ extern "C" int mtpb_attention_noalloc(const void* q, const void* k_cache, const 
   view.ml_elems = n_ml;
   view.o_elems = n_o;
   if (ns > 1) MTPB_CUDA(cudaMemsetAsync(view.counters, 0, n_ctr * 4, st));
-  return attn_run(dtype, q, k_cache, v_cache, out, B, T, hq, hkv, hd, cap, nullptr, cache_len, view,
-                  reinterpret_cast<uint32_t*>(base), st);
+  // device-side error bits go to the caller's word when it passes one
+  uint32_t* status_word = status ? status : reinterpret_cast<uint32_t*>(base);
+  return attn_run(dtype, q, k_cache, v_cache, out, B, T, hq, hkv, hd, cap, nullptr, cache_len, view, status_word,
+                  st);
 }

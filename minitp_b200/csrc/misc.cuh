@@ -403,4 +403,57 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* xv, const void
   }
 }
 
+// ---------------------------------------------------------------------------
+// NVLink latency floor: one LL word bounced between this rank and `peer`
+// `iters` times (one thread on each of the two ranks). The lower rank sends
+// ping i (sequence base + 2i) into the peer's buffer and waits for pong i
+// (base + 2i + 1) in its own; the peer answers each ping. ns_out gets the
+// time of the last `iters - warm` round trips on this rank. Every wait is
+// bounded by the communicator timeout (kStatusTimeout, then return). The
+// word sits at the start of this pair's channel-3 slot, with sequence
+// numbers of 2^31 and above, which no standalone collective uses.
+// ---------------------------------------------------------------------------
+struct PingParams {
+  Comm comm;
+  int peer;
+  int iters;
+  int warm;
+  uint32_t base;
+  unsigned long long* ns_out;
+};
+
+__global__ void pingpong_kernel(const PingParams p) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const Comm& c = p.comm;
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(c.data(c.rank, 3, 0, p.peer));
+  uint64_t* theirs = reinterpret_cast<uint64_t*>(c.data(p.peer, 3, 0, c.rank));
+  const bool lead = c.rank < p.peer;
+  uint64_t t0 = global_ns();
+  auto wait = [&](uint32_t seq) -> bool {
+    const uint64_t s0 = global_ns();
+    for (uint32_t n = 1;; ++n) {
+      if (ll_ld(mine).y == seq) return true;
+      if ((n & 63) == 0 && global_ns() - s0 > c.timeout_ns) return false;
+    }
+  };
+  for (int i = 0; i < p.iters; ++i) {
+    if (i == p.warm) t0 = global_ns();
+    const uint32_t ping = p.base + 2u * uint32_t(i), pong = ping + 1u;
+    if (lead) {
+      ll_put(theirs, 0u, ping);
+      if (!wait(pong)) {
+        atomicOr(c.status(), kStatusTimeout);
+        return;
+      }
+    } else {
+      if (!wait(ping)) {
+        atomicOr(c.status(), kStatusTimeout);
+        return;
+      }
+      ll_put(theirs, 0u, pong);
+    }
+  }
+  *p.ns_out = global_ns() - t0;
+}
+
 }  // namespace mtpb

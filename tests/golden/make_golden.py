@@ -339,10 +339,13 @@ def make_rope_goldens(ref_root: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MINITP_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MINITP_REFERENCE"),
+                    help="source tree of the reference (default: $MINITP_REFERENCE)")
     ap.add_argument("--only", nargs="*", default=None,
                     help="subset of: rope argmax embedding fused_ar " + " ".join(MODEL_RUNS))
     a = ap.parse_args()
+    if not a.reference:
+        raise SystemExit("give the reference source tree with --reference or $MINITP_REFERENCE")
     ref = os.path.abspath(a.reference)
     if not os.path.isdir(os.path.join(ref, "minitp")):
         raise SystemExit(f"reference package not found under {ref}")

@@ -106,7 +106,43 @@ def w_generate(rank, world, name, dtype, n_layers_override=0):
     out = generate_greedy(model, ids, n, early_stop=False)
     torch.cuda.synchronize()
     ctx.comm().raise_on_error()
-    return {"tokens": out.cpu().numpy(), "prefill_last_logits": logits[:, -1]}
+    return {"tokens": out.cpu().numpy(), "prefill_last_logits": logits[:, -1],
+            "decode_launches": np.array(decode_launches(model, b, p + n)),
+            "heads_padded": np.array(bool(model.cfg.is_padded))}
+
+
+def decode_launches(model, batch: int, cap: int) -> int:
+    """Kernel launches of one decode step as the library plans it (1 = the megakernel)."""
+    import ctypes
+
+    from minitp_b200 import _lib
+
+    nk = ctypes.c_int(0)
+    _lib.call("mtpb_model_decode_kernels", model.native(), batch, cap, ctypes.byref(nk))
+    return nk.value
+
+
+def w_teacher(rank, world, name, fixture):
+    """bf16 free-running ids plus teacher-forced decode top-2 (see tests/teacher.py)."""
+    from minitp_b200 import config as mcfg
+    from minitp_b200.generation import generate_greedy
+    from minitp_b200.weight_loader import load_synthetic_tp
+    from tests.teacher import teacher_forced_tops
+
+    cfgs = {"q05b": mcfg.qwen25_05b}
+    cfg = cfgs[name]()
+    g = np.load(os.path.join(REPO, "tests", "golden", fixture))
+    ctx = ctx_for(rank, world)
+    model = load_synthetic_tp(cfg, ctx, dtype=torch.bfloat16, device=ctx.device)
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    ref = torch.from_numpy(g["tokens"]).cuda()
+    n = g["top2_values"].shape[0]
+    out = generate_greedy(model, ids, n, early_stop=False)
+    vals, tids, _ = teacher_forced_tops(model, ids, ref, n)
+    torch.cuda.synchronize()
+    ctx.comm().raise_on_error()
+    return {"tokens": out.cpu().numpy(), "top_vals": vals, "top_ids": tids,
+            "decode_launches": np.array(decode_launches(model, ids.shape[0], ids.shape[1] + n))}
 
 
 def w_collectives(rank, world):

@@ -50,6 +50,24 @@ def decode_impl(request, lib):
     lib.mtpb_set_decode_impl(0)
 
 
+# Which fp32 TP=1 runs the decode megakernel plans (one launch per step). The
+# 7B shape at TP=1 in fp32 has 75 KB down_proj rows (18944 fp32) that, with
+# the activation buffers, exceed one CTA's shared memory: the library runs it
+# on the kernel chain, which the test asserts so the case cannot pass as a
+# megakernel run. Its megakernel coverage is the TP=4 multi-GPU test.
+MK_PLANS_FP32 = {"tiny": True, "q05b": True, "q05b_b4": True, "q7b_l2": False}
+
+
+def decode_launches(model, batch: int, cap: int) -> int:
+    import ctypes
+
+    from minitp_b200 import _lib
+
+    nk = ctypes.c_int(0)
+    _lib.call("mtpb_model_decode_kernels", model.native(), batch, cap, ctypes.byref(nk))
+    return nk.value
+
+
 @pytest.mark.parametrize("name", ["tiny", "q05b", "q05b_b4", "q7b_l2"])
 def test_fp32_tokens_and_logits(lib, name, decode_impl):
     from minitp_b200.generation import generate_greedy
@@ -57,6 +75,11 @@ def test_fp32_tokens_and_logits(lib, name, decode_impl):
     g = golden(f"model_{name}_tp1_fp32.npz")
     _, b, p, n = RUNS[name]
     model = _model(name, "fp32")
+    launches = decode_launches(model, b, p + n)
+    if decode_impl == 0:
+        assert (launches == 1) == MK_PLANS_FP32[name], f"{name}: decode step plans {launches} launches"
+    else:
+        assert launches > 1
     ids = torch.from_numpy(g["prompt"]).cuda()
     # prefill logits of the last position vs the reference
     logits = model(ids, positions=torch.arange(p, device="cuda")).float().cpu().numpy()[:, -1]
@@ -111,6 +134,35 @@ def test_megakernel_matches_chain_bf16(lib):
             ulp = 2.0 ** (np.floor(np.log2(abs(top[s, 0]))) - 7)
             assert top[s, 0] - top[s, 1] <= 4 * ulp, f"step {s} differs without a near-tie: {top[s]}"
     assert (logits[0] - logits[1]).abs().max().item() < 0.5
+
+
+@pytest.mark.parametrize("impl", [0, 1], ids=["megakernel", "chain"])
+def test_bf16_decode_logits_teacher_forced(lib, impl):
+    """bf16 decode-step logits against the reference (0.5B, TP=1).
+
+    Every decode step is fed the reference's own token, so the inputs stay
+    identical: decode step 1 and the last step are compared in full with the
+    reference's logits (0.5 absolute), every step's top logit with the
+    reference's top-2 record, and ids must agree except at near-ties.
+    """
+    from tests.teacher import check_teacher_tops, merge_rank_tops, teacher_forced_tops
+
+    g = golden("model_q05b_tp1_bf16.npz")
+    model = _model("q05b", "bf16")
+    ids = torch.from_numpy(g["prompt"]).cuda()
+    ref = torch.from_numpy(g["tokens"]).cuda()
+    n = g["top2_values"].shape[0]
+    lib.mtpb_set_decode_impl(impl)
+    try:
+        assert (decode_launches(model, 1, ids.shape[1] + n) == 1) == (impl == 0)
+        vals, tids, kept = teacher_forced_tops(model, ids, ref, n, keep_steps=(1, n - 1))
+    finally:
+        lib.mtpb_set_decode_impl(0)
+    model.ctx.comm().raise_on_error()
+    assert np.abs(kept[1] - g["decode1_logits"]).max() < 0.5
+    assert np.abs(kept[n - 1] - g["decode_last_logits"]).max() < 0.5
+    best, best_id = merge_rank_tops([vals], [tids])
+    check_teacher_tops(best, best_id, g["top2_values"], g["top2_ids"])
 
 
 @pytest.mark.parametrize("name", ["tiny", "q05b", "q7b_l2"])

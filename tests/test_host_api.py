@@ -154,10 +154,13 @@ def test_synthetic_protocol_matches_fixture_prompt():
 
 
 def test_launch_count_formula():
-    from bench import launches_per_generation
+    from bench import launches_per_generation, prefill_launch_count
 
-    # prefill: embed + 5 per layer + consume passes (2 per layer + final) + LM head;
+    # prefill: embed + 5 per layer + consume passes (2 per layer + final) + LM head
+    assert prefill_launch_count(2, 1, True) == 1 + 10 + 4 + 1 + 1
+    assert prefill_launch_count(2, 1, False) == 1 + 10 + 1
+    assert prefill_launch_count(2, 3, True) == 3 * (1 + 10 + 4) + 1 + 1
     # then argmax (2), the position seed (1) and the decode steps
-    assert launches_per_generation(2, 2, 8, 1 + 10 + 2) == (1 + 10 + 5 + 1) + 2 + 1 + (1 + 10 + 2)
+    assert launches_per_generation(17, 2, 1 + 10 + 2) == 17 + 2 + 1 + (1 + 10 + 2)
     # one decode megakernel launch per step
-    assert launches_per_generation(2, 5, 8, 1) == (1 + 10 + 5 + 1) + 2 + 1 + 4
+    assert launches_per_generation(17, 5, 1) == 17 + 2 + 1 + 4

@@ -54,11 +54,31 @@ def test_tp2_fp32_tokens_match_reference(name):
     g1 = golden(f"model_{name}_tp1_fp32.npz")
     for r in range(2):
         assert np.array_equal(res[r]["tokens"], g["tokens"]), r
+        assert int(res[r]["decode_launches"]) == 1  # the decode megakernel ran
     ref = g1["prefill_last_logits"]
     assert np.abs(res[0]["prefill_last_logits"] - ref).max() / np.abs(ref).max() < 1e-4
 
 
-def test_tp2_bf16_logits():
+def test_tp2_bf16_tokens_and_decode_logits_match_reference():
+    """0.5B bf16 at TP=2 against the reference's own TP=2 bf16 run.
+
+    Free-running ids equal the reference's up to its first near-tie; with the
+    reference's ids fed to every decode step, each step's top logit is within
+    0.5 of the reference's and the ids agree except at near-ties.
+    """
+    from tests.teacher import check_teacher_tops, check_tokens_up_to_near_tie, merge_rank_tops
+
+    res = mp_worker.run(2, mp_worker.w_teacher, "q05b", "model_q05b_tp2_bf16.npz")
+    g = golden("model_q05b_tp2_bf16.npz")
+    assert np.array_equal(res[0]["tokens"], res[1]["tokens"])
+    for r in range(2):
+        assert int(res[r]["decode_launches"]) == 1
+    check_tokens_up_to_near_tie(res[0]["tokens"], g["tokens"], g["top2_values"], g["prompt"].shape[1])
+    best, best_id = merge_rank_tops([x["top_vals"] for x in res], [x["top_ids"] for x in res])
+    check_teacher_tops(best, best_id, g["top2_values"], g["top2_ids"])
+
+
+def test_tp2_bf16_prefill_logits():
     res = mp_worker.run(2, mp_worker.w_generate, "q05b", "bf16")
     g1 = golden("model_q05b_tp1_bf16.npz")
     assert np.abs(res[0]["prefill_last_logits"] - g1["prefill_last_logits"]).max() < 0.5
@@ -79,3 +99,32 @@ def test_tp4_padded_tokens_match_tp1():
     g1 = golden("model_q05b_b4_tp1_fp32.npz")
     for r in range(4):
         assert np.array_equal(res[r]["tokens"], g1["tokens"]), r
+        assert bool(res[r]["heads_padded"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs >= 4 GPUs")
+def test_tp4_7b_tokens_match_reference_tp4():
+    """7B shape (2 layers, fp32) at TP=4: the reference's own TP=4 run (no padding, 1 KV head per rank)."""
+    res = mp_worker.run(4, mp_worker.w_generate, "q7b_l2", "fp32")
+    g = golden("model_q7b_l2_tp4_fp32.npz")
+    g1 = golden("model_q7b_l2_tp1_fp32.npz")
+    for r in range(4):
+        assert np.array_equal(res[r]["tokens"], g["tokens"]), r
+        assert int(res[r]["decode_launches"]) == 1
+        assert not bool(res[r]["heads_padded"])
+    ref = g1["prefill_last_logits"]
+    assert np.abs(res[0]["prefill_last_logits"] - ref).max() / np.abs(ref).max() < 1e-4
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
+def test_tp8_7b_padded_replicated_tokens_match_tp1():
+    """7B shape at TP=8, which the reference rejects (28 heads): Q heads padded to 32 and each
+    of the 4 KV heads replicated on 2 ranks. Tokens must equal the reference's TP=1 run."""
+    res = mp_worker.run(8, mp_worker.w_generate, "q7b_l2", "fp32")
+    g1 = golden("model_q7b_l2_tp1_fp32.npz")
+    for r in range(8):
+        assert np.array_equal(res[r]["tokens"], g1["tokens"]), r
+        assert int(res[r]["decode_launches"]) == 1
+        assert bool(res[r]["heads_padded"])
+    ref = g1["prefill_last_logits"]
+    assert np.abs(res[0]["prefill_last_logits"] - ref).max() / np.abs(ref).max() < 1e-4

@@ -124,3 +124,29 @@ def test_q05b_fp32_oracle_matches_reference_tokens():
     assert np.array_equal(out.numpy(), g["tokens"])
     ref = g["prefill_last_logits"]
     assert np.abs(kept[0].numpy() - ref).max() / np.abs(ref).max() < 1e-4
+
+
+def _w_oracle_rank(rank, world, name, dtype):
+    from minitp_b200 import config as mcfg
+    from oracle.model import OracleConfig, prompt
+    from oracle.rank import OracleRank
+
+    # q05b: the first 16 of the fixture's 128 greedy steps (a greedy run is prefix-consistent)
+    fac, b, p, n = {"tiny": (mcfg.baseline_tiny, 1, 8, 16), "q05b": (mcfg.qwen25_05b, 1, 128, 16)}[name]
+    cfg = OracleConfig.of(fac())
+    dt = torch.float32 if dtype == "fp32" else torch.bfloat16
+    m = OracleRank(cfg, rank, world, dtype=dt)
+    return m.generate(prompt(cfg.vocab_size, b, p), n).numpy()
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("name,tp,dtype", [("tiny", 1, "fp32"), ("tiny", 2, "fp32"), ("tiny", 2, "bf16"),
+                                           ("q05b", 2, "fp32")])
+def test_oracle_rank_gloo_matches_reference(name, tp, dtype):
+    """The per-rank Gloo restatement (the bench's reference arm) reproduces the reference's ids."""
+    from tests.tp_harness import run_tp
+
+    res = run_tp(tp, _w_oracle_rank, name, dtype)
+    g = golden(f"model_{name}_tp{tp}_{dtype}.npz")
+    for r in range(tp):
+        assert np.array_equal(res[r], g["tokens"][:, :res[r].shape[1]]), r
