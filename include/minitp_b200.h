@@ -265,12 +265,13 @@ int mtpb_model_decode_kernels(void* model, int B, int cap, int* launches);
  * shared-memory plan), 1 = the chain of per-operation kernels. */
 int mtpb_set_decode_impl(int impl);
 
-/* Diagnostic: when `buf` (device uint64[4096]) is not NULL, later megakernel
+/* Diagnostic: when `buf` (device uint64[16384]) is not NULL, later megakernel
  * launches record CTA 0's stage timeline there (%globaltimer ns): [0] start,
  * [1 + 12 l + e] the 12 stage events of layer l, [1 + 12 L ..] the LM-head and
  * selection events, [512 + s] the first weight copy of weight stage s,
  * [1000 ..] the phases of CTA 0's first attention item; the last CTA records
- * its stage events at [2048 + index]. */
+ * its stage events at [2048 + index], every CTA its layer-1 events at
+ * [4096 + 1024 e + cta]. */
 int mtpb_set_decode_trace(void* buf);
 
 /* Megakernel weight stream: chunks of at most `chunk_kb` KiB for the layers

@@ -16,7 +16,7 @@
 #include "gemv.cuh"
 #include "minitp_b200.h"
 #include "misc.cuh"
-#include "decode_mk.cuh"
+#include "decode_mk_launch.cuh"
 #include "gemm_tc.cuh"
 
 #include <cudaTypedefs.h>
@@ -853,6 +853,9 @@ int model_forward_t(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
 // ------------------------------------------------------------------ decode megakernel
 constexpr int kNotEligible = 1;
 
+// Row tile of the megakernel instantiation that serves M batch rows.
+int mk_row_tile(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
 int smem_optin() {
   int dev = 0, v = 0;
   cudaGetDevice(&dev);
@@ -888,6 +891,7 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   const int P = d.dtype == MTPB_BF16 ? 2 : 1;
   const int hd = d.head_dim;
   if (M < 1 || M > kMkMaxM) return kNotEligible;
+  if (!mk_has_variant(d.dtype == MTPB_BF16, mk_row_tile(M), d.head_dim)) return kNotEligible;
   // head_dim: a power of two in [16, 128] (lane-rotated 16-byte chunks)
   if (hd < 16 || hd > 128 || (hd & (hd - 1)) || d.hq_local % d.hkv_local) return kNotEligible;
   // 16-byte weight rows, and rows of whole LL pairs
@@ -987,28 +991,6 @@ int mk_reserve(ModelHost& mh) {
   return MTPB_OK;
 }
 
-template <typename T, int MT>
-int mk_launch_t(const MkParams& p, size_t smem, cudaStream_t st) {
-  auto kern = decode_mk_kernel<T, MT>;
-  static size_t smem_set = 0;  // the attribute is raised outside graph capture only
-  if (smem > smem_set) {
-    if (capturing(st)) return fail(MTPB_ERR_INVALID, "decode step: run one step eagerly before graph capture");
-    MTPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    smem_set = smem;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count());
-  cfg.blockDim = dim3(kMkThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  MTPB_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
-  return MTPB_OK;
-}
 
 // One decode step through the megakernel; kNotEligible when it cannot run it.
 int mk_decode(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
@@ -1052,20 +1034,15 @@ int mk_decode(ModelHost& mh, const FwdArgs& a, cudaStream_t st) {
   p.budget_ns = mh.comm->dev.timeout_ns;
   p.spin_ns = g_mk_spin_ns;
   p.trace = g_mk_trace;
-  const int MT = a.B <= 1 ? 1 : a.B <= 2 ? 2 : a.B <= 4 ? 4 : 8;
-  if (d.dtype == MTPB_BF16) {
-    switch (MT) {
-      case 1: return mk_launch_t<bf16, 1>(p, smem, st);
-      case 2: return mk_launch_t<bf16, 2>(p, smem, st);
-      case 4: return mk_launch_t<bf16, 4>(p, smem, st);
-      default: return mk_launch_t<bf16, 8>(p, smem, st);
-    }
-  }
-  switch (MT) {
-    case 1: return mk_launch_t<float, 1>(p, smem, st);
-    case 2: return mk_launch_t<float, 2>(p, smem, st);
-    case 4: return mk_launch_t<float, 4>(p, smem, st);
-    default: return mk_launch_t<float, 8>(p, smem, st);
+  const int MT = mk_row_tile(a.B);
+  cudaError_t err = cudaSuccess;
+  const int r = d.dtype == MTPB_BF16 ? mk_launch_bf16(MT, d.head_dim, p, sm_count(), smem, st, &err)
+                                     : mk_launch_f32(MT, d.head_dim, p, sm_count(), smem, st, &err);
+  switch (r) {
+    case kMkLaunchOk: return MTPB_OK;
+    case kMkLaunchNoVariant: return kNotEligible;
+    case kMkLaunchCapture: return fail(MTPB_ERR_INVALID, "decode step: run one step eagerly before graph capture");
+    default: return fail_cuda(err, "decode megakernel launch");
   }
 }
 

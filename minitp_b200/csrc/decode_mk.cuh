@@ -698,15 +698,20 @@ __device__ __forceinline__ bool mk_att_item(const MkCtx& c, const MkParams& p, c
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <typename T, int MT>
-__global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams p) {
+template <typename T, int MT, int HD>
+__global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkParams pk) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(16) MkParams p_s;
   __shared__ float red[32];
   __shared__ float kred[kMkCons * kMkMaxM * 4];
   __shared__ long long bests[kMkCons][kMkMaxM];
   __shared__ long long cta_best[kMkMaxM];
   __shared__ int ring_lo[kMkRingSlots], ring_hi[kMkRingSlots];  // ring range of a chunk in flight
   constexpr int P = LLPack<T>::kPer;
+  for (int i = threadIdx.x; i < int(sizeof(MkParams) / 4); i += blockDim.x)
+    reinterpret_cast<uint32_t*>(&p_s)[i] = reinterpret_cast<const uint32_t*>(&pk)[i];
+  __syncthreads();
+  const MkParams& p = p_s;
   const size_t tsz = sizeof(T);
   const MkLayout lay = mk_layout(p, tsz);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -1004,12 +1009,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const MkParams
             const bool tr = p.trace && blockIdx.x == 0 && li == 0;
             const uint32_t sp = uint32_t(l & 1), si = loc_seq(4 * l), so = loc_seq(4 * l + 1);
             T* vs = ks + stg_elems / 2;
-            switch (p.hd) {
-              case 16: ok = mk_att_item<T, 16>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-              case 32: ok = mk_att_item<T, 32>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-              case 64: ok = mk_att_item<T, 64>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-              default: ok = mk_att_item<T, 128>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr); break;
-            }
+            ok = mk_att_item<T, HD>(c, p, ly, it, t, pos, qs, ks, vs, sbar + li, sp, si, so, tr);
             __syncwarp();
           }
           if (!ok && lane == 0 && !*abort) mk_fail(c, p);

@@ -43,7 +43,7 @@ struct LLSpin {
   uint4 v;
   uint32_t ok;
 };
-__device__ __noinline__ LLSpin ll_spin_any(const uint64_t* src, uint32_t seq, int wide, uint64_t budget_ns,
+static __device__ __noinline__ LLSpin ll_spin_any(const uint64_t* src, uint32_t seq, int wide, uint64_t budget_ns,
                                            volatile int* abort, uint32_t backoff_ns) {
   LLSpin r;
   const uint64_t t0 = global_ns();
