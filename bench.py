@@ -376,10 +376,11 @@ def decode_bench(model, ctx, model_name, batch, prompt_len, new_tokens, args, fl
 
     def one_step():
         st = GenerationState(model, ids, new_tokens, session=sess)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record()
         logits = st.prefill(last_only=True)
         tok = st.select_next(logits)
+        ev[3].record()  # time to first token: prefill + greedy pick of its last position
         st.append(tok)
         st.start_device_decode(tok)
         replays = new_tokens - 1
@@ -407,7 +408,7 @@ def decode_bench(model, ctx, model_name, batch, prompt_len, new_tokens, args, fl
 
     sampler = ClockSampler(dev.index if dev.index is not None else 0)
     sampler.start()
-    decode_ms, step_ms = [], []
+    decode_ms, step_ms, ttft_ms = [], [], []
     barrier()
     for _ in range(args.steps):
         flush.zero_()  # L2 flush between timed steps (256 MiB > 126 MB L2)
@@ -415,15 +416,17 @@ def decode_bench(model, ctx, model_name, batch, prompt_len, new_tokens, args, fl
         torch.cuda.synchronize()
         decode_ms.append(ev[1].elapsed_time(ev[2]) / max(1, replays))
         step_ms.append(ev[0].elapsed_time(ev[2]))
+        ttft_ms.append(ev[0].elapsed_time(ev[3]))
         st.release()
     barrier()
     clocks = sampler.stop()
     ctx.comm().raise_on_error()
-    t = torch.tensor([statistics.mean(decode_ms), statistics.mean(step_ms)], dtype=torch.float64, device=dev)
+    t = torch.tensor([statistics.mean(decode_ms), statistics.mean(step_ms), statistics.mean(ttft_ms)],
+                     dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_per_token, ms_per_step = t.tolist()
-    res = {"batch": batch, "ms_per_token": ms_per_token, "ms_per_step": ms_per_step, "clocks": clocks,
+    ms_per_token, ms_per_step, ttft = t.tolist()
+    res = {"batch": batch, "ms_per_token": ms_per_token, "ms_per_step": ms_per_step, "ttft_ms": ttft, "clocks": clocks,
            "tok_s": batch / (ms_per_token / 1e3), "launches": decode_launches(model, batch, prompt_len + new_tokens),
            "prefill_launches": prefill_launches(model, batch, prompt_len, ctx.comm())}
     if with_e2e:
@@ -815,7 +818,8 @@ def run_b200(args):
         line = {
             "metric": "decode tok/s", "value": round(main["tok_s"], 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms_per_step"], 4),
-            "us_per_token": round(ms_per_token * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "us_per_token": round(ms_per_token * 1e3, 3), "ttft_ms": round(main["ttft_ms"], 3),
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.dtype,
             "data": "synthetic (seeded random weights N(0,0.02) and uniform prompt ids)",
             "config": {
@@ -854,6 +858,7 @@ def run_b200(args):
                 gbs = (wb + kv_r) / (r["ms_per_token"] / 1e3) / 1e9
                 line["batches"].append({
                     "batch": r["batch"], "tok_s": round(r["tok_s"], 2), "us_per_token": round(r["ms_per_token"] * 1e3, 3),
+                    "ttft_ms": round(r["ttft_ms"], 3),
                     "ms_per_step": round(r["ms_per_step"], 3), "decode_launches_per_token": r["launches"],
                     "decode_path": "megakernel" if r["launches"] == 1 else "kernel chain",
                     "roofline_frac": round(gbs / peak, 4), "bytes_per_token": round(wb + kv_r), "clocks": r["clocks"]})
