@@ -49,6 +49,11 @@ int mtpb_set_gemv_ctas_per_sm(int n);
 /* bf16 projections with at least `rows` rows (default 64) run on the tensor-core
  * (tcgen05) GEMM instead of the GEMV kernel; a large value keeps them on the GEMV. */
 int mtpb_set_tc_min_rows(int rows);
+/* The same threshold for the projections of a kernel-chain decode step (one
+ * row per batch row; default 8): from eight rows the CUDA-core GEMV runs short
+ * of registers and is compute-bound, while the tensor cores stay HBM-bound.
+ * No counterpart in the reference (a tuning switch of this library). */
+int mtpb_set_tc_min_rows_decode(int rows);
 
 /* Allow (1, default) or forbid (0) the CTA-pair tensor-core GEMM
  * (tcgen05 cta_group::2, 256 x 256 tiles on two SMs) for projections of at

@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_set_prefetch_cap": (c_int, [c_uint32]),
     "mtpb_set_gemv_ctas_per_sm": (c_int, [c_int]),
     "mtpb_set_tc_min_rows": (c_int, [c_int]),
+    "mtpb_set_tc_min_rows_decode": (c_int, [c_int]),
     "mtpb_set_tc_pair": (c_int, [c_int]),
     "mtpb_comm_create": (c_int, [c_int, c_int, c_uint64, POINTER(c_void_p)]),
     "mtpb_comm_ipc_handle": (c_int, [c_void_p, c_void_p]),

@@ -151,6 +151,9 @@ int gemv_launch(GemvParams p, cudaStream_t st) {
 // ------------------------------------------------------------------ tensor-core GEMM (prefill)
 bool capturing(cudaStream_t st);
 int g_tc_min_rows = 64;  // bf16 projections of at least this many rows use tcgen05
+// the same for the projections of a decode step (one row per batch row): the
+// CUDA-core GEMV turns compute-bound at a few tens of rows
+int g_tc_min_rows_decode = 8;
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -206,7 +209,8 @@ int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t col
 
 template <int EPI>
 bool tc_eligible(int dtype, const GemvParams& p) {
-  if (dtype != MTPB_BF16 || p.M < g_tc_min_rows || p.x_mode != 0 || !p.x) return false;
+  if (dtype != MTPB_BF16 || p.M < (p.decode ? g_tc_min_rows_decode : g_tc_min_rows) || p.x_mode != 0 || !p.x)
+    return false;
   if (EPI != kEpiStore && EPI != kEpiSwiglu && EPI != kEpiRope && EPI != kEpiPush) return false;
   if (p.K % 8 || p.ldx % 8 || p.K < kTcBK || !aligned16(p.x) || !aligned16(p.w)) return false;
   if (EPI == kEpiRope && (p.hd < 32 || p.hd > 128 || 128 % p.hd)) return false;
@@ -659,7 +663,10 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
   const int vloc = int(d.vocab_end - d.vocab_start);
   const uint32_t nsite = uint32_t(2 * L + 2);
   const bool chunked = tc != a.T;
-  const bool fused_x = size_t(M) * H * sizeof(T) <= kXsStageMax && tc == 1;
+  // decode steps of many rows take the tensor cores, which read x from global
+  // memory: no fused consume prologue for them
+  const bool tc_decode = a.decode && d.dtype == MTPB_BF16 && M >= g_tc_min_rows_decode;
+  const bool fused_x = size_t(M) * H * sizeof(T) <= kXsStageMax && tc == 1 && !tc_decode;
   const int chan = 0;
   const int pos_base = a.cache_len + t0;
   const long long* rope_pos = a.rope_pos ? a.rope_pos + t0 : nullptr;
@@ -732,6 +739,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
     // fused QKV + RoPE + KV append, consuming site 2l (embedding or previous down)
     {
       GemvParams g = gemv_base(ly.qkv_w, ly.qkv_b, M, qrows, H, qrows / 2);
+      g.decode = a.decode ? 1 : 0;
       MTPB_TRY(prepare_input(g, uint32_t(2 * l), ly.ln1, true));
       g.y = mh.q;
       g.ldy = hq * hd;
@@ -756,6 +764,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
     // o_proj partial -> push site 2l+1
     {
       GemvParams g = gemv_base(ly.o_w, nullptr, M, H, hq * hd, H);
+      g.decode = a.decode ? 1 : 0;
       g.x = mh.attn;
       g.ldx = hq * hd;
       g.comm = comm;
@@ -767,6 +776,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
     // gate/up + SwiGLU, consuming site 2l+1
     {
       GemvParams g = gemv_base(ly.gu_w, nullptr, M, 2 * d.inter_local, H, d.inter_local);
+      g.decode = a.decode ? 1 : 0;
       MTPB_TRY(prepare_input(g, uint32_t(2 * l + 1), ly.ln2, true));
       g.y = mh.act;
       g.ldy = d.inter_local;
@@ -775,6 +785,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
     // down partial -> push site 2l+2
     {
       GemvParams g = gemv_base(ly.down_w, nullptr, M, H, d.inter_local, H);
+      g.decode = a.decode ? 1 : 0;
       g.x = mh.act;
       g.ldx = d.inter_local;
       g.comm = comm;
@@ -791,6 +802,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
   {
     const int rows = a.last_only ? a.B : M;
     GemvParams g = gemv_base(d.lm_head, nullptr, rows, vloc, H, vloc);
+    g.decode = a.decode ? 1 : 0;
     const bool direct = fused_x && rows == M;
     MTPB_TRY(prepare_input(g, uint32_t(2 * L), d.final_norm, direct));
     if (!direct && a.last_only) {
@@ -1470,6 +1482,13 @@ int mtpb_set_tc_min_rows(int rows) {
   g_settings_epoch.fetch_add(1);
   if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
   g_tc_min_rows = rows;
+  return MTPB_OK;
+}
+
+int mtpb_set_tc_min_rows_decode(int rows) {
+  g_settings_epoch.fetch_add(1);
+  if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
+  g_tc_min_rows_decode = rows;
   return MTPB_OK;
 }
 

@@ -37,6 +37,7 @@ struct GemvParams {
   int M, N, K;
   int units;
   int ks;
+  int decode;  // a decode step's projection (T = 1): its own tensor-core row threshold
   // input
   int x_mode;  // 0: x from global memory; 1: consume a collective + RMSNorm
   const void* x;

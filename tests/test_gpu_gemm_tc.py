@@ -48,6 +48,27 @@ def test_tc_linear(lib, M, N, K):
     torch.testing.assert_close(y.float(), y2.float(), atol=1e-3, rtol=2 ** -7)
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 1152, 3584), (32, 3584, 4736), (48, 896, 896)])
+def test_tc_linear_few_rows(lib, M, N, K):
+    """Projections of 16-63 rows (a kernel-chain decode step at batch >= 16) on the tensor cores."""
+    from minitp_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 5 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    lib.mtpb_set_tc_min_rows(16)
+    try:
+        y = ops.linear(x.cuda(), w.cuda()).cpu()
+        s = ops.linear_swiglu(x.cuda(), w.cuda()).cpu()
+    finally:
+        lib.mtpb_set_tc_min_rows(64)
+    ref = _ref_linear(x, w)
+    torch.testing.assert_close(y.double(), ref.to(torch.bfloat16).double(), atol=1e-3, rtol=2 ** -7)
+    gate, up = torch.chunk(ref.to(torch.bfloat16), 2, dim=-1)
+    sref = F.silu(gate.float()).to(torch.bfloat16).float() * up.float()
+    torch.testing.assert_close(s.float(), sref.to(torch.bfloat16).float(), atol=1e-3, rtol=2 ** -6)
+
+
 @pytest.mark.parametrize("M,I,K", [(128, 2432, 896), (96, 200, 256), (1024, 4864, 896),
                                    (1000, 2500, 192)])
 def test_tc_swiglu(lib, M, I, K):

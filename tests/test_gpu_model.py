@@ -165,6 +165,51 @@ def test_bf16_decode_logits_teacher_forced(lib, impl):
     check_teacher_tops(best, best_id, g["top2_values"], g["top2_ids"])
 
 
+@pytest.mark.parametrize("batch", [8, 32])
+def test_chain_decode_batch_tensor_cores_match_gemv(lib, batch):
+    """7B shape (2 layers, bf16) at batch 8 and 32: the kernel-chain decode step
+    with its projections on the tensor cores (>= 8 rows) against the same step
+    on the CUDA-core GEMV. Both sum in fp32; logits within the bf16 tolerance
+    and the greedy ids equal except at near-ties of the GEMV run."""
+    from minitp_b200 import _lib
+    from minitp_b200.generation import GenerationState
+
+    model = _model("q7b_l2", "bf16")
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, model.cfg.vocab_size, (batch, 24), generator=g).cuda()
+    vloc = model.lm_head.weight.shape[0]
+    outs = []
+    for thr in (8, 1 << 30):
+        lib.mtpb_set_tc_min_rows_decode(thr)
+        try:
+            st = GenerationState(model, ids, 4)
+            tok = st.select_next(st.prefill(last_only=True))
+            st.append(tok)
+            st.start_device_decode(tok)
+            lg = torch.empty(batch, vloc, dtype=torch.bfloat16, device="cuda")
+            kp, vp = st.kv.pointer_arrays()
+            if batch > 8:
+                assert decode_launches(model, batch, st.kv.max_seq_len) > 1  # the kernel chain
+            _lib.call("mtpb_set_decode_impl", 1)  # the kernel chain at every batch
+            try:
+                _lib.call("mtpb_model_decode_step", model.native(), st._tok.data_ptr(), batch, kp, vp,
+                          st.kv.max_seq_len, None, 0, lg.data_ptr(), _lib.stream_ptr())
+            finally:
+                _lib.call("mtpb_set_decode_impl", 0)
+            torch.cuda.synchronize()
+            outs.append((lg.float().cpu(), st._tok.cpu().clone()))
+            st.release()
+        finally:
+            lib.mtpb_set_tc_min_rows_decode(8)
+    model.ctx.comm().raise_on_error()
+    (a, ta), (b, tb) = outs
+    assert (a - b).abs().max().item() < 0.5
+    top = torch.topk(b, 2, dim=-1).values
+    for r in torch.nonzero(ta != tb).flatten().tolist():
+        gap = (top[r, 0] - top[r, 1]).item()
+        assert gap <= 4 * 2.0 ** (np.floor(np.log2(abs(top[r, 0].item()))) - 7), f"row {r}: ids differ, gap {gap}"
+
+
 @pytest.mark.parametrize("name", ["tiny", "q05b", "q7b_l2"])
 def test_bf16_logits(lib, name):
     g = golden(f"model_{name}_tp1_bf16.npz")
