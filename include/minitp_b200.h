@@ -280,7 +280,8 @@ int mtpb_set_decode_impl(int impl);
 int mtpb_set_decode_trace(void* buf);
 
 /* Megakernel weight stream: chunks of at most `chunk_kb` KiB for the layers
- * (default 128) and `lm_chunk_kb` KiB for the LM head (default 96), in a
+ * (0, the default: 96 for one batch row when the ring holds two such chunks,
+ * else 128) and `lm_chunk_kb` KiB for the LM head (default 96), in a
  * shared-memory ring that takes the rest of the block's shared memory.
  * `l2_flags` bit 0: stream weights with an L2 evict-first policy; bit 1:
  * prefetch the next layer's weight rows into L2 (default 3, both). */

@@ -593,7 +593,7 @@ struct ModelHost {
 
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
-int g_mk_slot_kb = 128, g_mk_lm_kb = 96, g_mk_l2hint = 1, g_mk_l2ahead = 1;
+int g_mk_slot_kb = 0, g_mk_lm_kb = 96, g_mk_l2hint = 1, g_mk_l2ahead = 1;  // slot 0: automatic
 uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
@@ -932,7 +932,6 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   if (per_cta > kMkMaxStage) return kNotEligible;
   p.att_stage = per_cta;
   // stage kinds: units, their split over the CTAs, chunking
-  const size_t chunk_max = size_t(g_mk_slot_kb) * 1024;
   const size_t nq = size_t(d.hq_local + 2 * d.hkv_local) * hd;
   const size_t hvec = mk_align(size_t(d.hidden) * tsz);
   struct KindShape {
@@ -954,6 +953,12 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   const int budget = smem_optin() - 4096;  // static shared memory of the kernel
   p.ring_bytes = 0;
   const size_t fixed = mk_layout(p, tsz).ring;
+  // layer chunk cap: 96 KiB for one row when the ring holds two such chunks
+  // (the next layer's gate/up chunk then lands while this layer's down
+  // chunk is consumed), else 128 KiB; a set value overrides it
+  size_t chunk_max = size_t(g_mk_slot_kb) * 1024;
+  if (g_mk_slot_kb == 0)
+    chunk_max = (M == 1 && size_t(budget) > fixed + 176 * 1024) ? 96 * 1024 : 128 * 1024;
   size_t biggest = 0;
   for (size_t cap = chunk_max;; cap -= 16 * 1024) {
     biggest = 0;
@@ -1468,8 +1473,9 @@ int mtpb_model_destroy(void* model) {
 
 int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
   g_settings_epoch.fetch_add(1);
-  if (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4 || lm_chunk_kb < 4 || lm_chunk_kb > 200 || lm_chunk_kb % 4)
-    return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4");
+  if ((chunk_kb != 0 && (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4)) || lm_chunk_kb < 4 || lm_chunk_kb > 200 ||
+      lm_chunk_kb % 4)
+    return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4 (layer chunks: 0 = automatic)");
   if (l2_flags < 0 || l2_flags > 3) return fail(MTPB_ERR_INVALID, "decode ring: l2 flags 0..3");
   g_mk_slot_kb = chunk_kb;
   g_mk_lm_kb = lm_chunk_kb;

@@ -62,6 +62,7 @@ constexpr int kMkHdr = 1024;      // shared-memory header: mbarriers + control w
 // Copies of the words that every CTA reads (merged attention output, act):
 // CTA b reads copy b % kMkRep, so fewer CTAs poll any one line.
 constexpr int kMkRep = 4;
+constexpr int kMkMergeLoads = 4;  // split outputs a merge lane loads per round
 
 // GEMV stage kinds
 enum : int { kMkQkv = 0, kMkO = 1, kMkGu = 2, kMkDown = 3, kMkLm = 4, kMkKinds = 5 };
@@ -1023,11 +1024,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
         }
       } else {
       {
-          const int hd = p.hd, hd2 = hd / 2, pairs = p.M * p.hq;
+          // one warp per (row, head, block of 32 dim pairs): head dims above
+          // 64 take several warps, each its own dims of every split
+          const int hd = p.hd, hd2 = hd / 2, ndb = (hd2 + 31) / 32, items = p.M * p.hq * ndb;
           const uint32_t seq = loc_seq(4 * l + 1), hseq = loc_seq(4 * l + 2);
           const size_t head_n = size_t(p.M) * (p.hq * hd / P);
           bool ok = !*abort;
-          for (int pr = blockIdx.x + G * c.cw; pr < pairs && ok; pr += G * kMkCons) {
+          for (int wi = blockIdx.x + G * c.cw; wi < items && ok; wi += G * kMkCons) {
+            const int pr = wi / ndb, db = wi - pr * ndb;
             const uint64_t* part = p.att_ll + size_t(pr) * nsp * (hd + 2);
             uint4 a[2];
             a[0] = make_uint4(__float_as_uint(-INFINITY), seq, 0u, seq);
@@ -1054,16 +1058,20 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
             const int m = pr / p.hq, hh = pr - m * p.hq;
             // every lane runs every iteration (the shuffles need the whole warp);
             // lanes past the head's dim pairs load and store nothing
-            for (int dp0 = 0; dp0 < hd2; dp0 += 32) {
-              const int dp = dp0 + lane;
+            {
+              const int dp = db * 32 + lane;
               const bool act = dp < hd2;
               float o[2] = {0.f, 0.f};
-              for (int s0 = 0; s0 < nsp; s0 += 4) {
-                uint4 v[4];
+              // every split's (max, sum) has arrived, so its outputs have too:
+              // kMkMergeLoads loads per round
+              for (int s0 = 0; s0 < nsp; s0 += kMkMergeLoads) {
+                uint4 v[kMkMergeLoads];
                 auto addr = [&](int u) { return part + size_t(s0 + u) * (hd + 2) + 2 * dp; };
-                if (act && ok && !ll_wait2<4>(p.budget_ns, p.spin_ns, addr, min(4, nsp - s0), seq, v, abort)) ok = false;
+                if (act && ok &&
+                    !ll_wait2<kMkMergeLoads>(p.budget_ns, p.spin_ns, addr, min(kMkMergeLoads, nsp - s0), seq, v, abort))
+                  ok = false;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < kMkMergeLoads; ++u) {
                   const int sidx = s0 + u;
                   if (sidx < nsp) {
                     const float ws = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
