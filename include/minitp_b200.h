@@ -280,9 +280,11 @@ int mtpb_set_decode_impl(int impl);
 int mtpb_set_decode_trace(void* buf);
 
 /* Megakernel weight stream: chunks of at most `chunk_kb` KiB for the layers
- * (0, the default: 96 for one batch row when the ring holds two such chunks,
- * else 128) and `lm_chunk_kb` KiB for the LM head (default 96), in a
- * shared-memory ring that takes the rest of the block's shared memory.
+ * and `lm_chunk_kb` KiB for the LM head, in a shared-memory ring that takes
+ * the rest of the block's shared memory. 0 (the default for both) chooses
+ * them per shape: the LM head, and layers whose weights per CTA exceed two
+ * ring-fulls, take half the ring (two chunks in flight); other layers 96
+ * KiB for one batch row when the ring holds two, else 128.
  * `l2_flags` bit 0: stream weights with an L2 evict-first policy; bit 1:
  * prefetch the next layer's weight rows into L2 (default 3, both). */
 int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags);

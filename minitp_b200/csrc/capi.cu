@@ -593,7 +593,7 @@ struct ModelHost {
 
 int g_decode_impl = 0;  // 0: megakernel when the shape allows it, 1: kernel chain
 unsigned long long* g_mk_trace = nullptr;  // stage timeline buffer of the megakernel (device)
-int g_mk_slot_kb = 0, g_mk_lm_kb = 96, g_mk_l2hint = 1, g_mk_l2ahead = 1;  // slot 0: automatic
+int g_mk_slot_kb = 0, g_mk_lm_kb = 0, g_mk_l2hint = 1, g_mk_l2ahead = 1;  // chunk caps 0: automatic
 uint32_t g_mk_spin_ns = 0;
 
 bool capturing(cudaStream_t st) {
@@ -953,12 +953,26 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   const int budget = smem_optin() - 4096;  // static shared memory of the kernel
   p.ring_bytes = 0;
   const size_t fixed = mk_layout(p, tsz).ring;
-  // layer chunk cap: 96 KiB for one row when the ring holds two such chunks
-  // (the next layer's gate/up chunk then lands while this layer's down
-  // chunk is consumed), else 128 KiB; a set value overrides it
+  // Chunk caps. The ring is what is left of shared memory. A stage whose
+  // weights per CTA are many ring-fulls is bound by the weight stream: its
+  // chunks take half the ring, so one lands while the other is consumed (the
+  // LM head always; a layer when its bytes per CTA exceed two rings).
+  // Otherwise a layer streams in chunks of 96 KiB for one row when the ring
+  // holds two (the next layer's gate/up lands while this layer's down is
+  // consumed), else 128 KiB. Set values override the automatic ones.
+  const size_t ring_est = size_t(budget) > fixed ? size_t(budget) - fixed : 0;
+  const size_t half_ring = std::max<size_t>(16 * 1024, (ring_est / 2) & ~size_t(16 * 1024 - 1));
+  size_t layer_bytes = 0;  // weight bytes of one layer per CTA
+  for (int k = 0; k < kMkLm; ++k)
+    layer_bytes += (size_t(ks[k].units) + G - 1) / G * ks[k].halves * ks[k].rpu * size_t(ks[k].K) * tsz;
   size_t chunk_max = size_t(g_mk_slot_kb) * 1024;
-  if (g_mk_slot_kb == 0)
-    chunk_max = (M == 1 && size_t(budget) > fixed + 176 * 1024) ? 96 * 1024 : 128 * 1024;
+  if (g_mk_slot_kb == 0) {
+    if (layer_bytes > 2 * ring_est)
+      chunk_max = std::min<size_t>(128 * 1024, half_ring);
+    else
+      chunk_max = (M == 1 && ring_est > 176 * 1024) ? 96 * 1024 : 128 * 1024;
+  }
+  const size_t lm_max = g_mk_lm_kb > 0 ? size_t(g_mk_lm_kb) * 1024 : std::min<size_t>(96 * 1024, half_ring);
   size_t biggest = 0;
   for (size_t cap = chunk_max;; cap -= 16 * 1024) {
     biggest = 0;
@@ -973,7 +987,7 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
       kd.pre = int(ks[k].pre);
       const size_t ub = size_t(kd.halves) * kd.rpu * kd.K * tsz;
       // the LM head streams in smaller chunks: more of them in flight
-      const size_t cmax = k == kMkLm ? std::min(cap, size_t(g_mk_lm_kb) * 1024) : cap;
+      const size_t cmax = k == kMkLm ? std::min(cap, lm_max) : cap;
       const size_t room = cmax > ks[k].pre ? cmax - ks[k].pre : 0;
       kd.upc = int(std::max<size_t>(1, room / ub));
       biggest = std::max(biggest, ks[k].pre + size_t(kd.upc) * ub);
@@ -1473,9 +1487,9 @@ int mtpb_model_destroy(void* model) {
 
 int mtpb_set_decode_ring(int chunk_kb, int lm_chunk_kb, int l2_flags) {
   g_settings_epoch.fetch_add(1);
-  if ((chunk_kb != 0 && (chunk_kb < 4 || chunk_kb > 200 || chunk_kb % 4)) || lm_chunk_kb < 4 || lm_chunk_kb > 200 ||
-      lm_chunk_kb % 4)
-    return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4 (layer chunks: 0 = automatic)");
+  auto bad = [](int kb) { return kb != 0 && (kb < 4 || kb > 200 || kb % 4); };
+  if (bad(chunk_kb) || bad(lm_chunk_kb))
+    return fail(MTPB_ERR_INVALID, "decode ring: chunk sizes in [4, 200] KiB, multiples of 4, or 0 = automatic");
   if (l2_flags < 0 || l2_flags > 3) return fail(MTPB_ERR_INVALID, "decode ring: l2 flags 0..3");
   g_mk_slot_kb = chunk_kb;
   g_mk_lm_kb = lm_chunk_kb;

@@ -122,23 +122,25 @@ def _iter_layer_slices(cfg: ModelConfig, rank: int, tp: int, get) -> Iterator[tu
         p = f"model.layers.{i}."
         a, m = p + "self_attn.", p + "mlp."
         yield p + "input_layernorm.weight", get(p + "input_layernorm.weight", "full", 0, 0)
-        qw, qb = [], []
-        for head in q_heads:
-            if head < 0:
-                qw.append(torch.zeros(hd, h))
-                qb.append(torch.zeros(hd))
-            else:
-                qw.append(get(a + "q_proj.weight", "rows", head * hd, hd))
-                qb.append(get(a + "q_proj.bias", "rows", head * hd, hd))
         kw = get(a + "k_proj.weight", "rows", kv_start, kv_len)
         vw = get(a + "v_proj.weight", "rows", kv_start, kv_len)
         kb = get(a + "k_proj.bias", "rows", kv_start, kv_len)
         vb = get(a + "v_proj.bias", "rows", kv_start, kv_len)
+        # padded heads: zeros on the device and in the dtype of the source tensors
+        zeros = lambda *shape: torch.zeros(*shape, dtype=kw.dtype, device=kw.device)  # noqa: E731
+        qw, qb = [], []
+        for head in q_heads:
+            if head < 0:
+                qw.append(zeros(hd, h))
+                qb.append(zeros(hd))
+            else:
+                qw.append(get(a + "q_proj.weight", "rows", head * hd, hd))
+                qb.append(get(a + "q_proj.bias", "rows", head * hd, hd))
         yield a + "qkv_proj.weight", torch.cat([*qw, kw, vw], dim=0)
         yield a + "qkv_proj.bias", torch.cat([*qb, kb, vb], dim=0)
         ocols = []
         for head in q_heads:
-            ocols.append(torch.zeros(h, hd) if head < 0 else get(a + "o_proj.weight", "cols", head * hd, hd))
+            ocols.append(zeros(h, hd) if head < 0 else get(a + "o_proj.weight", "cols", head * hd, hd))
         yield a + "o_proj.weight", torch.cat(ocols, dim=1)
         yield p + "post_attention_layernorm.weight", get(p + "post_attention_layernorm.weight", "full", 0, 0)
         gate = get(m + "gate_proj.weight", "rows", inter_start, inter_len)

@@ -164,3 +164,32 @@ def test_launch_count_formula():
     assert launches_per_generation(17, 2, 1 + 10 + 2) == 17 + 2 + 1 + (1 + 10 + 2)
     # one decode megakernel launch per step
     assert launches_per_generation(17, 5, 1) == 17 + 2 + 1 + 4
+
+
+def test_padded_heads_follow_the_source_tensors():
+    """Zero rows of padded Q heads take the device and dtype of the checkpoint tensors
+    (weights drawn on a GPU must not meet CPU zeros)."""
+    from minitp_b200.weight_loader import _iter_layer_slices
+
+    cfg = ModelConfig(64, 128, 1, 6, 2, 8, 50, 1e-6, 1e6, 64, True).padded_for(4)
+
+    def get(name, kind, a, b):  # stand-in source: bf16 tensors of the right shapes
+        shapes = {"model.embed_tokens.weight": (50, 64), "k_proj.weight": (16, 64), "v_proj.weight": (16, 64),
+                  "k_proj.bias": (16,), "v_proj.bias": (16,), "q_proj.weight": (48, 64), "q_proj.bias": (48,),
+                  "o_proj.weight": (64, 48), "gate_proj.weight": (128, 64), "up_proj.weight": (128, 64),
+                  "down_proj.weight": (64, 128)}
+        key = next((k for k in shapes if name.endswith(k)), None)
+        full = torch.ones(shapes[key] if key else (64,), dtype=torch.bfloat16)
+        if kind == "rows":
+            return full[a:a + b]
+        if kind == "cols":
+            return full[:, a:a + b]
+        return full
+
+    padded = 0
+    for r in range(4):
+        for key, t in _iter_layer_slices(cfg, r, 4, get):
+            assert t.dtype == torch.bfloat16, key
+            if key.endswith("qkv_proj.weight"):
+                padded += int((t == 0).all(dim=1).sum())
+    assert padded > 0  # some rank holds zero (padded) head rows
