@@ -997,7 +997,10 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   }
   p.ring_bytes = int((size_t(budget) - fixed) & ~size_t(127));
   p.l2_hint = g_mk_l2hint;
-  p.l2_ahead = g_mk_l2ahead;
+  // the next layer's rows go into L2 ahead of time only when a layer's weights
+  // of this rank fit in well under half the L2 (126 MB): larger layers would
+  // evict what the current one still needs
+  p.l2_ahead = g_mk_l2ahead && layer_bytes * size_t(G) <= (48u << 20);
   *smem_out = mk_layout(p, tsz).total;
   const MkScratch sl = mk_scratch_layout(d);
   if (mh.mk_bytes < sl.total) return kNotEligible;  // reserved by mk_reserve

@@ -782,6 +782,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
         int u0, nu;
         mk_units(kd, u0, nu);
         const uint32_t rb = uint32_t(kd.K) * uint32_t(tsz), hb1 = uint32_t(kd.rpu) * rb;
+        int pf_upto = 0;  // units of this stage already prefetched into L2 while the ring was full
         // a stage with vectors in front has at least one chunk, even without units
         for (int cc = 0; (cc < nu || (cc == 0 && kd.pre)) && !stop; cc += kd.upc) {
           const int n = max(0, min(kd.upc, nu - cc));
@@ -789,11 +790,22 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
           const uint32_t B = pre + uint32_t(kd.halves * n) * hb1;
           const int at = head + int(B) <= p.ring_bytes ? head : 0;
           // room: fewer than kMkRingSlots chunks in flight, none overlapping [at, at + B)
-          for (;;) {
+          for (bool first = true;; first = false) {
             bool fit = k - k_old < kMkRingSlots;
             for (int i = k_old; i < k && fit; ++i)
               fit = at + int(B) <= ring_lo[i & (kMkRingSlots - 1)] || at >= ring_hi[i & (kMkRingSlots - 1)];
             if (fit) break;
+            if (first) {
+              // the ring is full: start this chunk's rows and the next chunk's on
+              // their way into L2, so the copies are L2 hits once room frees
+              const int u_end = min(nu, cc + 2 * kd.upc);
+              if (pf_upto < u_end) {
+                const int ub = max(pf_upto, cc);
+                for (int h = 0; h < kd.halves; ++h)
+                  bulk_prefetch_l2(w + (size_t(h) * kd.hoff + size_t(u0 + ub) * kd.rpu) * rb, uint32_t(u_end - ub) * hb1);
+                pf_upto = u_end;
+              }
+            }
             if (!mbar_wait(empty + (k_old & (kMkRingSlots - 1)), uint32_t(k_old / kMkRingSlots) & 1u, p.budget_ns,
                            abort)) {
               *abort = 1;
