@@ -62,6 +62,18 @@ int mtpb_set_tc_min_rows_decode(int rows);
  * tuning switch of this library). */
 int mtpb_set_tc_pair(int enable);
 
+/* Most K ranges per output tile of the single-CTA tensor-core GEMM (split K,
+ * default 32; 1 turns it off); returns the previous value, -1 outside
+ * [1, 64]. A projection whose output tiles fill at most half of the SMs
+ * splits its K blocks into ranges (at least two 64-column blocks each, at
+ * most one item per SM); partials go to a per-device fp32 workspace (about
+ * 64 KB per SM, allocated on the first split call, which must not be under
+ * graph capture) and are summed in range order by the last arriving CTA, so
+ * results do not depend on timing. Split GEMMs of one device must not run
+ * concurrently on two streams (they share that workspace). No counterpart in
+ * the reference (a tuning switch of this library). */
+int mtpb_set_tc_split(int max_splits);
+
 /* ------------------------------------------------------- communicator
  * Peer-memory communicator over NVLink (one per rank; TP group == world).
  * Replaces the torch.distributed process group used by the hot-path

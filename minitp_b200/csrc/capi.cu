@@ -231,13 +231,42 @@ int tc_tiles_n(const GemvParams& p, int bn) {
 // else 128 wide (more CTAs on the small-M, HBM-bound shapes). Persistent
 // grids: one CTA per SM at most.
 struct TcPlan {
-  int pair;  // 1: gemm_tc2_kernel (cta_group::2)
-  int bn;    // single-CTA tile width
+  int pair;    // 1: gemm_tc2_kernel (cta_group::2)
+  int bn;      // single-CTA tile width
   int tiles_m, tiles_n;
+  int splits;  // K ranges per tile (single CTAs, BN 128)
   int grid;
 };
 
-int g_tc_pair = 1;  // CTA-pair kernel allowed
+int g_tc_pair = 1;       // CTA-pair kernel allowed
+int g_tc_split_max = 32;  // most K ranges per output tile (1: no split K)
+
+// Split-K workspace of a device: fp32 partial tiles for at most one item per
+// SM (a split plan never has more items than SMs) and one arrival counter per
+// tile (zero between launches; the kernel returns each to zero). One set per
+// device, so split GEMMs on one device run one at a time (one stream).
+struct TcSplitWs {
+  float* ws = nullptr;
+  int* cnt = nullptr;
+};
+
+int tc_split_ws(cudaStream_t st, TcSplitWs* out) {
+  static std::mutex mu;
+  static TcSplitWs per_dev[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  TcSplitWs& w = per_dev[dev];
+  if (!w.ws) {
+    if (capturing(st)) return fail(MTPB_ERR_INVALID, "tensor-core GEMM: run one call eagerly before graph capture");
+    const size_t items = size_t(sm_count());
+    MTPB_CUDA(cudaMalloc(&w.ws, items * kTcBM * 128 * sizeof(float)));
+    MTPB_CUDA(cudaMalloc(&w.cnt, items * sizeof(int)));
+    MTPB_CUDA(cudaMemset(w.cnt, 0, items * sizeof(int)));
+  }
+  *out = w;
+  return MTPB_OK;
+}
 
 // Per-epilogue one-time setup: shared-memory limits of the three kernels and
 // the number of co-resident CTA pairs (their shared memory allows one CTA per
@@ -297,10 +326,17 @@ TcPlan tc_plan(const GemvParams& p) {
     pl.grid = 2 * std::min(tm2 * tn2, pairs);
     return pl;
   }
+  const int sms = sm_count();
   pl.tiles_m = (p.M + kTcBM - 1) / kTcBM;
-  pl.bn = pl.tiles_m * tc_tiles_n<EPI>(p, 256) >= sm_count() ? 256 : 128;
+  pl.bn = pl.tiles_m * tc_tiles_n<EPI>(p, 256) >= sms ? 256 : 128;
   pl.tiles_n = tc_tiles_n<EPI>(p, pl.bn);
-  pl.grid = std::min(pl.tiles_m * pl.tiles_n, sm_count());
+  // split K when the tiles fill at most half of the SMs: as many ranges as
+  // keep every item within one per SM, each of at least two K blocks
+  const int tiles = pl.tiles_m * pl.tiles_n, nk = (p.K + kTcBK - 1) / kTcBK;
+  pl.splits = 1;
+  if (pl.bn == 128 && g_tc_split_max > 1 && 2 * tiles <= sms)
+    pl.splits = std::max(1, std::min(std::min(sms / tiles, nk / 2), g_tc_split_max));
+  pl.grid = std::min(tiles * pl.splits, sms);
   return pl;
 }
 
@@ -334,6 +370,15 @@ int gemm_tc_launch(const GemvParams& g, cudaStream_t st) {
   tp.g = g;
   tp.tiles_m = pl.tiles_m;
   tp.tiles_n = pl.tiles_n;
+  tp.splits = pl.pair ? 1 : pl.splits;
+  tp.ws = nullptr;
+  tp.cnt = nullptr;
+  if (tp.splits > 1) {
+    TcSplitWs w;
+    MTPB_TRY(tc_split_ws(st, &w));
+    tp.ws = w.ws;
+    tp.cnt = w.cnt;
+  }
   tp.budget_ns = 2000000000ull;
   // W boxes: a CTA of a pair loads 128 rows; a single CTA BN rows (SwiGLU: two halves)
   const uint32_t wbox = pl.pair ? 128u : uint32_t(EPI == kEpiSwiglu ? pl.bn / 2 : pl.bn);
@@ -927,6 +972,8 @@ int mk_plan(ModelHost& mh, int M, int cap, MkParams& p, size_t* smem_out) {
   p.nsplit = ns;
   p.xin_cols = std::max(d.hq_local * hd, d.inter_local);
   p.wsc_floats = kMkCons * 3 * hd;
+  // the QKV bias of a CTA's units is kept in shared memory
+  if (((d.hq_local + 2 * d.hkv_local) * hd / P + G - 1) / G * P > kMkBiasMax) return kNotEligible;
   // every attention item of a CTA is staged in shared memory
   const int per_cta = (M * d.hq_local * ns + G - 1) / G;
   if (per_cta > kMkMaxStage) return kNotEligible;
@@ -1513,6 +1560,14 @@ int mtpb_set_tc_min_rows_decode(int rows) {
   if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
   g_tc_min_rows_decode = rows;
   return MTPB_OK;
+}
+
+int mtpb_set_tc_split(int max_splits) {
+  g_settings_epoch.fetch_add(1);
+  if (max_splits < 1 || max_splits > 64) return -1;
+  const int prev = g_tc_split_max;
+  g_tc_split_max = max_splits;
+  return prev;
 }
 
 int mtpb_set_tc_pair(int enable) {

@@ -63,6 +63,7 @@ constexpr int kMkHdr = 1024;      // shared-memory header: mbarriers + control w
 // CTA b reads copy b % kMkRep, so fewer CTAs poll any one line.
 constexpr int kMkRep = 4;
 constexpr int kMkMergeLoads = 4;  // split outputs a merge lane loads per round
+constexpr int kMkBiasMax = 256;   // QKV bias values of one CTA's units
 
 // GEMV stage kinds
 enum : int { kMkQkv = 0, kMkO = 1, kMkGu = 2, kMkDown = 3, kMkLm = 4, kMkKinds = 5 };
@@ -188,7 +189,7 @@ __device__ __forceinline__ bool ll_spin2(const MkParams& p, const uint64_t* src,
   } while (0)
 
 struct MkLayout {
-  size_t lys, xres, xnorm, xin, wsc, stg, ring, total;
+  size_t lys, xres, xnorm, xin, wsc, bias, stg, ring, total;
 };
 
 __host__ __device__ inline size_t mk_align(size_t x) { return (x + 127) & ~size_t(127); }
@@ -210,6 +211,8 @@ __host__ __device__ inline MkLayout mk_layout(const MkParams& p, size_t tsz) {
   off = mk_align(off + size_t(p.M) * p.xin_cols * tsz);
   l.wsc = off;
   off = mk_align(off + size_t(p.wsc_floats) * sizeof(float));
+  l.bias = off;
+  off = mk_align(off + size_t(kMkBiasMax) * sizeof(float));
   l.stg = off;
   off = mk_align(off + size_t(p.att_stage) * mk_stage_bytes(p, tsz));
   l.ring = off;
@@ -484,10 +487,11 @@ __device__ __forceinline__ void cons_gemv_chunk(const MkCtx& c, const char* rows
 
 // Epilogue of a layer's GEMV stage: what happens to the outputs of unit u.
 struct MkEpi {
-  int kind;         // kMkQkv, kMkO, kMkGu or kMkDown
-  uint32_t seq;     // sequence number of the words it writes
-  int site;         // AllReduce site (O, down)
-  const void* bias; // QKV bias (shared memory) or null
+  int kind;           // kMkQkv, kMkO, kMkGu or kMkDown
+  uint32_t seq;       // sequence number of the words it writes
+  int site;           // AllReduce site (O, down)
+  const float* bias;  // QKV bias of this CTA's units (shared memory) or null
+  int bias_u0;        // first unit of that slice
 };
 
 // One chunk of a layer's GEMV stage with its epilogue (QKV, O and down share
@@ -512,9 +516,8 @@ __device__ __forceinline__ void mk_stage_chunk(MkCtx c, const MkParams& p, MkEpi
 #pragma unroll
       for (int q = 0; q < kMkRep; ++q) ll_put(p.act_ll + q * act_n + size_t(m) * (p.I / P) + u, wd, e.seq);
     } else if (e.kind == kMkQkv) {
-      const T* bias = static_cast<const T*>(e.bias);
 #pragma unroll
-      for (int k = 0; k < P; ++k) r[k] = bias ? v[k] + to_f(bias[u * P + k]) : v[k];
+      for (int k = 0; k < P; ++k) r[k] = e.bias ? v[k] + e.bias[(u - e.bias_u0) * P + k] : v[k];
       const int nq = (p.hq + 2 * p.hkv) * p.hd;
       ll_put(p.qkv_ll + size_t(m) * (nq / P) + u, LLPack<T>::pack(r), e.seq);
     } else {
@@ -725,6 +728,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   T* xnorm = reinterpret_cast<T*>(smem + lay.xnorm);
   T* xin = reinterpret_cast<T*>(smem + lay.xin);
   float* wsc = reinterpret_cast<float*>(smem + lay.wsc);
+  float* qkv_bias_s = reinterpret_cast<float*>(smem + lay.bias);  // this CTA's QKV bias values
   T* stg = reinterpret_cast<T*>(smem + lay.stg);
   char* ring = reinterpret_cast<char*>(smem + lay.ring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -982,7 +986,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     //   4 gather head outputs       5 O       6 reduce (site 2l+1) + ln2
     //   7 gate/up                   8 gather act             9 down
     uint32_t first_off = 0;   // ring offset of the chunk that carries the gain
-    const T* qkv_bias = nullptr;
+    const float* qkv_bias = nullptr;
+    int qkv_u0 = 0;
     for (int ph = 0; ph < 10 * p.L && alive; ++ph) {
       const int l = ph / 10, k = ph - 10 * l;
       const MkLayer& ly = lys[l];
@@ -992,7 +997,19 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
         first_off = chunk_wait();
         if (k == 6) MK_TRACE(c, p, tb + 3);  // the gate/up chunk (with ln2) has landed
         const T* gain = reinterpret_cast<const T*>(ring + first_off);
-        if (k == 0) qkv_bias = ly.qkv_b ? reinterpret_cast<const T*>(ring + first_off + hvec) : nullptr;
+        if (k == 0 && ly.qkv_b) {
+          // this CTA's slice of the QKV bias leaves the ring now: the chunk
+          // that carries it is released after the stage's first chunk, while
+          // the epilogue of later chunks still needs it (the barrier that ends
+          // the reduce below orders these stores before the QKV stage)
+          const T* rb = reinterpret_cast<const T*>(ring + first_off + hvec);
+          int nu;
+          mk_units(p.kinds[kMkQkv], qkv_u0, nu);
+          for (int i = c.tid; i < nu * P; i += kMkConsThreads) qkv_bias_s[i] = to_f(rb[size_t(qkv_u0) * P + i]);
+          qkv_bias = qkv_bias_s;
+        } else if (k == 0) {
+          qkv_bias = nullptr;
+        }
         const int site = 2 * l + (k == 6 ? 1 : 0);
         alive = cons_reduce_norm<T>(c, p, site, site_seq(site), k == 6 || l > 0, gain, xres, xnorm);
         MK_TRACE(c, p, tb + (k == 0 ? 1 : 8));
@@ -1004,6 +1021,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
         e.site = kind == kMkO ? 2 * l + 1 : 2 * l + 2;
         e.seq = kind == kMkQkv ? loc_seq(4 * l) : kind == kMkGu ? loc_seq(4 * l + 3) : site_seq(e.site);
         e.bias = kind == kMkQkv ? qkv_bias : nullptr;
+        e.bias_u0 = qkv_u0;
         run_stage(kind, from_norm ? int(first_off) : -1, from_norm ? xnorm : xin, from_norm ? H : p.xin_cols, e);
         MK_TRACE(c, p, tb + (k == 1 ? 2 : k == 5 ? 7 : k == 7 ? 9 : 11));
       } else if (k == 4 || k == 8) {

@@ -16,6 +16,15 @@
 // next. Every wait is bounded; on expiry the CTA records a status bit, lets
 // its copies and MMAs land, frees its tensor memory and returns.
 //
+// Split K (single-CTA kernel, BN 128): when there are too few output tiles
+// to occupy the SMs, each tile's K blocks are cut into `splits` consecutive
+// ranges, one work item each. An item's epilogue writes its fp32 partial
+// accumulator to a workspace, publishes it (fence + a per-tile arrival
+// counter) and the CTA that completes the count sums the tile's partials in
+// split order 0, 1, ... (the same order whichever CTA arrives last, so the
+// result does not depend on timing) and runs the epilogue on the sum; it
+// also returns the counter to zero for the next launch.
+//
 // Output units follow the GEMV epilogue: SwiGLU pairs gate row u with up row
 // I + u, so its W tile is loaded as two BN/2-row halves (gate rows, then the
 // matching up rows); RoPE pairs rows i and i + hd/2 of a head, which a tile of
@@ -51,8 +60,16 @@ struct TcCfg {
 struct TcParams {
   GemvParams g;  // shapes, inputs and epilogue fields (GEMV conventions)
   int tiles_m, tiles_n;
+  int splits;    // K ranges per output tile (1: no split; > 1 only with BN 128)
+  float* ws;     // split partials: [tile][split][BN / 4][128 rows][4] fp32
+  int* cnt;      // per-tile arrival counters, zero between launches
   uint64_t budget_ns;
 };
+
+// Offset (floats) of accumulator column c (multiple of 4) of tile row r in
+// one split partial: four consecutive columns of 128 rows are 2 KB, so the 32
+// lanes (rows) of a warp store and load 512 consecutive bytes.
+__device__ __forceinline__ size_t tc_ws_off(int c, int r) { return (size_t(c >> 2) * kTcBM + r) * 4; }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -154,8 +171,10 @@ __device__ __forceinline__ void tc_epi_rows(const GemvParams& p, int row0, int r
 // [part * U/2, (part + 1) * U/2) of rows row0 .. row0 + 31, where trow is the
 // tensor-memory address of the warp's lane quarter in the accumulator, U the
 // units per tile and u_tile the first unit of the tile.
-template <typename T, int EPI, int BN>
-__device__ __forceinline__ void tc_epilogue_tile(const GemvParams& p, uint32_t trow, int row0, int u_tile, int part,
+// ld16(col, r) fetches 16 consecutive accumulator columns of this lane's row
+// (tensor memory, or the sum of the split partials).
+template <typename T, int EPI, int BN, typename Ld>
+__device__ __forceinline__ void tc_epilogue_tile(const GemvParams& p, const Ld& ld16, int row0, int u_tile, int part,
                                                  float* bufa, float* bufb, int lane, uint32_t out_seq) {
   constexpr bool kPair = EPI == kEpiSwiglu || EPI == kEpiRope;
   constexpr int kUnitsPerTile = kPair ? BN / 2 : BN;
@@ -163,11 +182,11 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemvParams& p, uint32_t t
   const int bound = EPI == kEpiSwiglu ? (p.N >> 1) : EPI == kEpiRope ? (p.hq + 2 * p.hkv) * (hd >> 1) : p.N;
   for (int q0 = part * (kUnitsPerTile / 2); q0 < (part + 1) * (kUnitsPerTile / 2); q0 += 32) {
     uint32_t ra[32], rb[32];
-    tc_ld16(trow + tc_col_a<EPI, BN>(q0, hd), ra);
-    tc_ld16(trow + tc_col_a<EPI, BN>(q0 + 16, hd), ra + 16);
+    ld16(tc_col_a<EPI, BN>(q0, hd), ra);
+    ld16(tc_col_a<EPI, BN>(q0 + 16, hd), ra + 16);
     if constexpr (kPair) {
-      tc_ld16(trow + tc_col_b<EPI, BN>(q0, hd), rb);
-      tc_ld16(trow + tc_col_b<EPI, BN>(q0 + 16, hd), rb + 16);
+      ld16(tc_col_b<EPI, BN>(q0, hd), rb);
+      ld16(tc_col_b<EPI, BN>(q0 + 16, hd), rb + 16);
     }
     tc_wait_ld();
 #pragma unroll
@@ -202,6 +221,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* xpose = reinterpret_cast<float*>(smem_raw + (base - smem_u32(smem_raw)) + size_t(S) * C::kStageBytes);
   const int nk = (p.K + kTcBK - 1) / kTcBK;
   const int tiles = tp.tiles_m * tp.tiles_n;
+  const int splits = tp.splits;
+  const int items = tiles * splits;  // item i: tile i / splits, K range i % splits
+  __shared__ int last_sh;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -237,9 +259,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- TMA producer
     if (lane == 0) {
       int g = 0;
-      for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+      for (int it = blockIdx.x; it < items && !*abort; it += gridDim.x) {
+        const int t = it / splits, sp = it - t * splits;
         const int tm = t % tp.tiles_m, tn = t / tp.tiles_m;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = sp * nk / splits; kb < (sp + 1) * nk / splits; ++kb, ++g) {
           const int s = g % S;
           if (g >= S && !mbar_wait(empty + s, uint32_t((g / S) & 1) ^ 1u, tp.budget_ns, abort)) {
             *abort = 1;
@@ -264,7 +287,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- MMA issuer
     if (lane == 0) {
       int g = 0, i = 0;
-      for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++i) {
+      for (int it = blockIdx.x; it < items && !*abort; it += gridDim.x, ++i) {
+        const int sp = it % splits;
+        const int kb0 = sp * nk / splits;
         const int b = i & 1, use = i >> 1;
         if (use > 0 && !mbar_wait(acc_empty + b, uint32_t((use - 1) & 1), tp.budget_ns, abort)) {
           *abort = 1;
@@ -273,7 +298,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + uint32_t(b * BN);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
+        for (int kb = kb0; kb < (sp + 1) * nk / splits; ++kb, ++g) {
           const int s = g % S;
           if (!mbar_wait(full + s, uint32_t((g / S) & 1), tp.budget_ns, abort)) {
             *abort = 1;
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t sa = base + uint32_t(s) * C::kStageBytes, sb = sa + kTcABytes;
 #pragma unroll
           for (int k = 0; k < kTcBK / 16; ++k)
-            tc_mma(acc, tc_smem_desc(sa + k * 32), tc_smem_desc(sb + k * 32), C::kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma(acc, tc_smem_desc(sa + k * 32), tc_smem_desc(sb + k * 32), C::kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           tc_commit(empty + s);  // the stage is free once these MMAs have read it
         }
         if (!ok) break;
@@ -298,22 +323,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float* bufa = xpose + size_t(ew) * (2 * 32 * kTcXs);
     float* bufb = bufa + 32 * kTcXs;
     int i = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++i) {
+      const int t = it / splits;
       const int b = i & 1, use = i >> 1;
       const int tm = t % tp.tiles_m, tn = t / tp.tiles_m;
+      const int row0 = tm * kTcBM + quarter * 32;
       const bool ok = mbar_wait(acc_full + b, uint32_t(use & 1), tp.budget_ns, abort);
-      if (!__all_sync(0xffffffffu, ok)) {
+      // split items meet at CTA barriers below: there all epilogue warps leave together
+      if (splits > 1 ? !named_sync_and(2, 32 * kTcEpiWarps, __all_sync(0xffffffffu, ok))
+                     : !__all_sync(0xffffffffu, ok)) {
         if (lane == 0) *abort = 1;
         break;
       }
       tc_fence_after();
       const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * BN);
-      tc_epilogue_tile<T, EPI, BN>(p, trow, tm * kTcBM + quarter * 32, tn * kUnitsPerTile, part, bufa, bufb, lane,
-                                   out_seq);
-      // the accumulator may be overwritten once every epilogue warp has read it
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty + b);
+      if (splits == 1) {
+        auto ld_tmem = [&](int col, uint32_t* r) { tc_ld16(trow + uint32_t(col), r); };
+        tc_epilogue_tile<T, EPI, BN>(p, ld_tmem, row0, tn * kUnitsPerTile, part, bufa, bufb, lane, out_seq);
+        // the accumulator may be overwritten once every epilogue warp has read it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + b);
+        continue;
+      }
+      if constexpr (BN == 128) {
+        // this item's partial: the warp's 32 rows x BN / 2 columns, rows of x only
+        const int r = quarter * 32 + lane;
+        const bool row_ok = tm * kTcBM + r < p.M;
+        if (row0 < p.M) {
+          float* dst = tp.ws + size_t(it) * (kTcBM * BN);
+#pragma unroll
+          for (int c0 = part * (BN / 2); c0 < (part + 1) * (BN / 2); c0 += 16) {
+            uint32_t v[16];
+            tc_ld16(trow + uint32_t(c0), v);
+            tc_wait_ld();
+            if (row_ok) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(dst + tc_ws_off(c0 + j, r)) =
+                    make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                __uint_as_float(v[j + 3]));
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + b);
+        // publish: every writer's stores ordered before the count
+        __threadfence();
+        named_sync(1, 32 * kTcEpiWarps);
+        if (warp == 2 && lane == 0) {
+          const int prev = atomicAdd(tp.cnt + t, 1);
+          const int last = prev == splits - 1;
+          if (last) tp.cnt[t] = 0;
+          last_sh = last;
+        }
+        named_sync(1, 32 * kTcEpiWarps);
+        if (!last_sh || row0 >= p.M) continue;
+        __threadfence();
+        const float* src = tp.ws + size_t(t) * splits * (kTcBM * BN);
+        auto ld_sum = [&](int col, uint32_t* out) {
+          float a[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) a[j] = 0.f;
+          if (row_ok) {
+#pragma unroll 4
+            for (int q = 0; q < splits; ++q) {
+              const float* ps = src + size_t(q) * (kTcBM * BN);
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 f = __ldcg(reinterpret_cast<const float4*>(ps + tc_ws_off(col + j, r)));
+                a[j] += f.x;
+                a[j + 1] += f.y;
+                a[j + 2] += f.z;
+                a[j + 3] += f.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) out[j] = __float_as_uint(a[j]);
+        };
+        tc_epilogue_tile<T, EPI, BN>(p, ld_sum, row0, tn * kUnitsPerTile, part, bufa, bufb, lane, out_seq);
+      }
     }
   }
   __syncwarp();
@@ -535,7 +626,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_after();
       const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * BN);
-      tc_epilogue_tile<T, EPI, BN>(p, trow, tm * 256 + int(crank) * kTcBM + quarter * 32, tn * kUnitsPerTile, part,
+      auto ld_tmem = [&](int col, uint32_t* r) { tc_ld16(trow + uint32_t(col), r); };
+      tc_epilogue_tile<T, EPI, BN>(p, ld_tmem, tm * 256 + int(crank) * kTcBM + quarter * 32, tn * kUnitsPerTile, part,
                                    bufa, bufb, lane, out_seq);
       tc_fence_before();
       __syncwarp();

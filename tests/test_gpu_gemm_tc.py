@@ -7,7 +7,8 @@ epilogues, full and partial tiles, K that is not a multiple of the 64-element
 K block, both tile widths of the single-CTA kernel (128 and 256 accumulator
 columns), the CTA-pair kernel (256 x 256 tiles, cta_group::2: projections of
 >= 256 rows with at least one tile per co-resident pair), and persistent CTAs
-that take several tiles each (both tensor-memory accumulators in turn).
+that take several tiles each (both tensor-memory accumulators in turn), and
+split K for projections with few output tiles.
 """
 
 import pytest
@@ -67,6 +68,38 @@ def test_tc_linear_few_rows(lib, M, N, K):
     gate, up = torch.chunk(ref.to(torch.bfloat16), 2, dim=-1)
     sref = F.silu(gate.float()).to(torch.bfloat16).float() * up.float()
     torch.testing.assert_close(s.float(), sref.to(torch.bfloat16).float(), atol=1e-3, rtol=2 ** -6)
+
+
+@pytest.mark.parametrize("epi,M,N,K", [("store", 8, 768, 3584), ("store", 32, 896, 4864), ("swiglu", 8, 4736, 3584),
+                                       ("store", 128, 1152, 896), ("store", 8, 3584, 512), ("swiglu", 64, 2000, 200)])
+def test_tc_split_k(lib, epi, M, N, K):
+    """Split K (output tiles filling at most half of the SMs): the float64 reference, the unsplit kernel
+    within the same tolerance, and bit-identical results on repeated calls (partials summed in range order)."""
+    from minitp_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 3 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    fn = ops.linear_swiglu if epi == "swiglu" else ops.linear
+    lib.mtpb_set_tc_min_rows(1)
+    try:
+        y1 = fn(x, w).cpu()
+        y2 = fn(x, w).cpu()
+        prev = lib.mtpb_set_tc_split(1)
+        try:
+            y0 = fn(x, w).cpu()
+        finally:
+            lib.mtpb_set_tc_split(prev)
+    finally:
+        lib.mtpb_set_tc_min_rows(64)
+    assert torch.equal(y1, y2)
+    ref = _ref_linear(x.cpu(), w.cpu()).to(torch.bfloat16)
+    if epi == "swiglu":
+        gate, up = torch.chunk(ref, 2, dim=-1)
+        ref = (F.silu(gate.float()).to(torch.bfloat16).float() * up.float()).to(torch.bfloat16)
+    tol = dict(atol=1e-3, rtol=2 ** -6)
+    torch.testing.assert_close(y1.float(), ref.float(), **tol)
+    torch.testing.assert_close(y1.float(), y0.float(), **tol)
 
 
 @pytest.mark.parametrize("M,I,K", [(128, 2432, 896), (96, 200, 256), (1024, 4864, 896),

@@ -90,6 +90,26 @@ def test_fp32_tokens_and_logits(lib, name, decode_impl):
     assert np.array_equal(got, g["tokens"]), f"first mismatch at {np.argwhere(got != g['tokens'])[:3].tolist()}"
 
 
+@pytest.mark.parametrize("name", ["q05b_b4", "tiny"])
+def test_megakernel_small_weight_chunks(lib, name):
+    """fp32 tokens with 16 KiB weight chunks: every GEMV stage of a CTA spans several ring chunks and the
+    ring wraps within a stage (the QKV bias and norm gains travel in a stage's first chunk only)."""
+    from minitp_b200.generation import generate_greedy
+
+    g = golden(f"model_{name}_tp1_fp32.npz")
+    _, b, p, n = RUNS[name]
+    model = _model(name, "fp32")
+    assert lib.mtpb_set_decode_ring(16, 16, 3) == 0
+    try:
+        assert decode_launches(model, b, p + n) == 1
+        out = generate_greedy(model, torch.from_numpy(g["prompt"]).cuda(), n, early_stop=False)
+    finally:
+        lib.mtpb_set_decode_ring(0, 0, 3)
+    model.ctx.comm().raise_on_error()
+    got = out.cpu().numpy()
+    assert np.array_equal(got, g["tokens"]), f"first mismatch at {np.argwhere(got != g['tokens'])[:3].tolist()}"
+
+
 def test_megakernel_matches_chain_bf16(lib):
     """Both decode implementations agree in bf16 (0.5B shape).
 
