@@ -74,6 +74,22 @@ int mtpb_set_tc_pair(int enable);
  * the reference (a tuning switch of this library). */
 int mtpb_set_tc_split(int max_splits);
 
+/* Two-shot form of the model's AllReduce sites that are not fused into a
+ * projection (prefill chunks, decode steps of many rows): reduce-scatter,
+ * then all-gather (each rank reduces one column slice of every row and sends
+ * the result to the others) for messages of at least min_bytes on at least
+ * min_world ranks; smaller ones stay one-shot (every rank pushes its whole
+ * partial to every peer). Defaults 262144 bytes and 4 ranks; min_bytes < 0
+ * turns it off. Both forms sum in rank order with the same rounding, so
+ * results are identical. The standalone mtpb_allreduce* calls stay one-shot.
+ * No counterpart in the reference (a tuning switch of this library). */
+int mtpb_set_allreduce_two_shot(long long min_bytes, int min_world);
+
+/* The form the library picks for a model AllReduce site of `bytes` bytes in
+ * rows of H values on `world` ranks: the column slice width of the two-shot
+ * form, or 0 for one-shot. No counterpart in the reference. */
+int mtpb_allreduce_two_shot_cols(long long bytes, int H, int world, int dtype);
+
 /* ------------------------------------------------------- communicator
  * Peer-memory communicator over NVLink (one per rank; TP group == world).
  * Replaces the torch.distributed process group used by the hot-path

@@ -69,6 +69,8 @@ SIGNATURES: dict[str, tuple] = {
     "mtpb_set_tc_min_rows_decode": (c_int, [c_int]),
     "mtpb_set_tc_pair": (c_int, [c_int]),
     "mtpb_set_tc_split": (c_int, [c_int]),
+    "mtpb_set_allreduce_two_shot": (c_int, [c_int64, c_int]),
+    "mtpb_allreduce_two_shot_cols": (c_int, [c_int64, c_int, c_int, c_int]),
     "mtpb_comm_create": (c_int, [c_int, c_int, c_uint64, POINTER(c_void_p)]),
     "mtpb_comm_ipc_handle": (c_int, [c_void_p, c_void_p]),
     "mtpb_comm_open": (c_int, [c_void_p, c_void_p]),

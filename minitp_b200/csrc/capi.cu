@@ -16,6 +16,7 @@
 #include "gemv.cuh"
 #include "minitp_b200.h"
 #include "misc.cuh"
+#include "ar_rows.cuh"
 #include "decode_mk_launch.cuh"
 #include "gemm_tc.cuh"
 
@@ -531,6 +532,24 @@ int embed_run(int dtype, const EmbedParams& p, int grid, cudaStream_t st) {
   return fail(MTPB_ERR_INVALID, "unsupported dtype");
 }
 
+// Two-shot AllReduce sites of the model (reduce-scatter + all-gather,
+// comm.cuh) for messages of at least g_ts_min_bytes on at least
+// g_ts_min_world ranks: each rank then sends 2 (tp - 1) / tp of the message
+// instead of (tp - 1) copies, for one more flag round trip.
+long long g_ts_min_bytes = 256 * 1024;
+int g_ts_min_world = 4;
+
+// Column slice width of a two-shot site of rows of H values (0: one-shot).
+int ts_cols_for(size_t bytes, int H, int world, int dtype) {
+  if (g_ts_min_bytes < 0 || world < std::max(2, g_ts_min_world) || bytes < size_t(g_ts_min_bytes)) return 0;
+  if (!(dtype == MTPB_BF16 ? ar_rows_vec_ok<bf16>(H) : ar_rows_vec_ok<float>(H))) return 0;
+  // producer and consumer grids stay below the all-gather flag indices
+  if (sm_count() * std::max(2, g_gemv_ctas_per_sm) > kAgCta) return 0;
+  const int VE = vec_elems(dtype);
+  const int per = (H + world - 1) / world;
+  return (per + VE - 1) / VE * VE;
+}
+
 int ar_norm_run(int dtype, ArNormParams p, cudaStream_t st) {
   if (size_t(p.rows) * p.H * dsize(dtype) > p.comm.slot_bytes && p.comm.world > 1)
     return fail(MTPB_ERR_INVALID, "allreduce: message larger than the communicator slot");
@@ -567,8 +586,36 @@ int argmax_rows_run(int dtype, const ArgmaxRowsParams& p, cudaStream_t st) {
 struct ConsumeRowsParams {
   GemvParams g;  // x_mode-1 fields (comm, seq, res_in, res_out, gain, eps, M, K = H)
   void* xn;      // [M][H]
+  int ts_cols;   // > 0: a two-shot site (slices of ts_cols columns, see comm.cuh)
 };
 
+// Vector form (H a multiple of the 16-byte vector, at most kArRowVecs
+// vectors per thread): row m on CTA m % grid, the same on every rank, which
+// the two-shot all-gather relies on (CTA b waits only for CTA b of each rank).
+template <typename T>
+__global__ void __launch_bounds__(kArRowThreads) consume_rows_vec_kernel(const ConsumeRowsParams cp) {
+  __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
+  const GemvParams& p = cp.g;
+  const Comm& c = p.comm;
+  const uint32_t seq = resolve_seq(c, p.in_seq);
+  if (!wait_peers(c, p.in_chan, seq, p.in_nprod)) return;
+  const int par = seq & 1;
+  const int H = p.K;
+  const int ts = c.world > 1 ? cp.ts_cols : 0;
+  if (ts > 0) {
+    for (int m = blockIdx.x; m < p.M; m += gridDim.x) ar_reduce_slice<T>(c, p.in_chan, par, ts, m, H);
+    signal_peers_at(c, p.in_chan, seq, kAgCta + blockIdx.x);
+    if (!wait_peers_cta(c, p.in_chan, seq, kAgCta + blockIdx.x)) return;
+  }
+  for (int m = blockIdx.x; m < p.M; m += gridDim.x)
+    ar_finish_row<T>(c, p.in_chan, par, ts, nullptr, m, H, static_cast<const T*>(p.ar_bias),
+                     p.has_res ? static_cast<const T*>(p.res_in) : nullptr, static_cast<T*>(p.res_out),
+                     static_cast<const T*>(p.gain), p.eps, static_cast<T*>(cp.xn), red);
+}
+
+// Scalar form (any H; one-shot sites only).
 template <typename T>
 __global__ void __launch_bounds__(256) consume_rows_kernel(const ConsumeRowsParams cp) {
   __shared__ float red[32];
@@ -608,8 +655,14 @@ __global__ void __launch_bounds__(256) consume_rows_kernel(const ConsumeRowsPara
 
 int consume_rows_run(int dtype, const ConsumeRowsParams& cp, cudaStream_t st) {
   const int grid = std::max(1, std::min(cp.g.M, sm_count() * 2));
-  if (dtype == MTPB_BF16) return launch(consume_rows_kernel<bf16>, dim3(grid), dim3(256), 0, st, cp);
-  if (dtype == MTPB_F32) return launch(consume_rows_kernel<float>, dim3(grid), dim3(256), 0, st, cp);
+  const bool vec = dtype == MTPB_BF16 ? ar_rows_vec_ok<bf16>(cp.g.K) : ar_rows_vec_ok<float>(cp.g.K);
+  if (cp.ts_cols > 0 && (!vec || grid > kAgCta)) return fail(MTPB_ERR_INVALID, "two-shot site: unsupported row shape");
+  if (dtype == MTPB_BF16)
+    return vec ? launch(consume_rows_vec_kernel<bf16>, dim3(grid), dim3(kArRowThreads), 0, st, cp)
+               : launch(consume_rows_kernel<bf16>, dim3(grid), dim3(256), 0, st, cp);
+  if (dtype == MTPB_F32)
+    return vec ? launch(consume_rows_vec_kernel<float>, dim3(grid), dim3(kArRowThreads), 0, st, cp)
+               : launch(consume_rows_kernel<float>, dim3(grid), dim3(256), 0, st, cp);
   return fail(MTPB_ERR_INVALID, "unsupported dtype");
 }
 
@@ -712,6 +765,8 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
   // memory: no fused consume prologue for them
   const bool tc_decode = a.decode && d.dtype == MTPB_BF16 && M >= g_tc_min_rows_decode;
   const bool fused_x = size_t(M) * H * sizeof(T) <= kXsStageMax && tc == 1 && !tc_decode;
+  // sites consumed by the separate pass may take the two-shot form
+  const int ts = fused_x ? 0 : ts_cols_for(size_t(M) * H * sizeof(T), H, comm.world, d.dtype);
   const int chan = 0;
   const int pos_base = a.cache_len + t0;
   const long long* rope_pos = a.rope_pos ? a.rope_pos + t0 : nullptr;
@@ -770,6 +825,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
       cp.g.M = M;
       cp.g.K = H;
       cp.xn = mh.xn;
+      cp.ts_cols = ts;
       MTPB_TRY(consume_rows_run(d.dtype, cp, st));
       g.x_mode = 0;
       g.x = mh.xn;
@@ -815,6 +871,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
       g.comm = comm;
       g.out_seq = SeqRef{uint32_t(2 * l + 1), nsite, 0u};
       g.out_chan = chan;
+      g.ts_cols = ts;
       MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
       nprod = push_grid(d.dtype, g);
     }
@@ -836,6 +893,7 @@ int model_chunk_t(ModelHost& mh, const FwdArgs& a, int t0, int tc, bool last_chu
       g.comm = comm;
       g.out_seq = SeqRef{uint32_t(2 * l + 2), nsite, 0u};
       g.out_chan = chan;
+      g.ts_cols = ts;
       MTPB_TRY(gemv_dispatch<kEpiPush>(d.dtype, g, st));
       nprod = push_grid(d.dtype, g);
     }
@@ -1560,6 +1618,19 @@ int mtpb_set_tc_min_rows_decode(int rows) {
   if (rows < 1) return fail(MTPB_ERR_INVALID, "tensor-core GEMM row threshold must be >= 1");
   g_tc_min_rows_decode = rows;
   return MTPB_OK;
+}
+
+int mtpb_set_allreduce_two_shot(long long min_bytes, int min_world) {
+  g_settings_epoch.fetch_add(1);
+  if (min_world < 2) return fail(MTPB_ERR_INVALID, "two-shot allreduce: min_world must be >= 2");
+  g_ts_min_bytes = min_bytes;
+  g_ts_min_world = min_world;
+  return MTPB_OK;
+}
+
+int mtpb_allreduce_two_shot_cols(long long bytes, int H, int world, int dtype) {
+  if (bytes < 0 || H <= 0 || world < 1) return 0;
+  return ts_cols_for(size_t(bytes), H, world, dtype);
 }
 
 int mtpb_set_tc_split(int max_splits) {

@@ -91,6 +91,33 @@ __device__ __forceinline__ void signal_peers(const Comm& c, int chan, uint32_t s
   }
 }
 
+// Two-shot form (reduce-scatter, then all-gather) of a large collective: the
+// columns of a row are cut into `world` slices of ts_cols columns (a multiple
+// of the vector width; the last slice may be short or empty) and rank j owns
+// slice j. Producers store slice j of their partial rows only into rank j's
+// data[chan][par][src] (one copy of each value instead of `world`). Consumer
+// CTA b of the owner sums its rows' slice over the sources in rank order,
+// rounds it like the one-shot sum, and stores the result into the unused
+// slice-j columns of data[chan][par][j] on every rank, then raises flag
+// kAgCta + b; every rank's CTA b waits for those flags and reads each column
+// from the slot of its owner. Consumers of both forms compute identical bits.
+constexpr int kAgCta = 512;  // flag index offset of the all-gather step
+
+__host__ __device__ inline int ts_owner(int col, int ts_cols, int world) {
+  const int j = col / ts_cols;
+  return j < world ? j : world - 1;
+}
+
+// Producer side, explicit flag index: raise flag `cta` on every rank.
+__device__ __forceinline__ void signal_peers_at(const Comm& c, int chan, uint32_t seq, int cta) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_sys();
+    const int par = seq & 1;
+    for (int d = 0; d < c.world; ++d) st_relaxed_sys(c.flag(d, chan, par, c.rank, cta), seq);
+  }
+}
+
 // Consumer side: wait until producer CTAs [0, nprod) of every rank signalled
 // `seq`. With world == 1 nothing needs waiting (stream order suffices).
 // (warp 0 polls; every thread of the block must call it)

@@ -63,6 +63,20 @@ __device__ __forceinline__ void unpack(const uint4& u, float (&f)[4]) {
   f[3] = __uint_as_float(u.w);
 }
 
+// Pack fp32 lanes into one 16-byte vector of the storage type (round to
+// nearest even for bf16).
+__device__ __forceinline__ uint4 pack_vec(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]))) |
+           (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]))) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ uint4 pack_vec(const float (&f)[4]) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+}
+
 // Streaming 16-byte load of read-only data (weights): no L1 allocation.
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   uint4 v;

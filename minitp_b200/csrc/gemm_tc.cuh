@@ -379,29 +379,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           last_sh = last;
         }
         named_sync(1, 32 * kTcEpiWarps);
-        if (!last_sh || row0 >= p.M) continue;
+        if (!last_sh) continue;
         __threadfence();
-        const float* src = tp.ws + size_t(t) * splits * (kTcBM * BN);
-        auto ld_sum = [&](int col, uint32_t* out) {
-          float a[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) a[j] = 0.f;
-          if (row_ok) {
-#pragma unroll 4
-            for (int q = 0; q < splits; ++q) {
-              const float* ps = src + size_t(q) * (kTcBM * BN);
-#pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                const float4 f = __ldcg(reinterpret_cast<const float4*>(ps + tc_ws_off(col + j, r)));
-                a[j] += f.x;
-                a[j + 1] += f.y;
-                a[j + 2] += f.z;
-                a[j + 3] += f.w;
-              }
-            }
+        // the tile's sum, by all epilogue threads (one float4 of a row each,
+        // consecutive threads on consecutive rows), into split 0's partial
+        float* sum = tp.ws + size_t(t) * splits * (kTcBM * BN);
+        const int rows_t = min(kTcBM, p.M - tm * kTcBM), n4 = rows_t * (BN / 4);
+        for (int e4 = int(threadIdx.x) - 64; e4 < n4; e4 += 32 * kTcEpiWarps) {
+          const int rr = e4 % rows_t, c4 = e4 / rows_t;
+          float4* a0 = reinterpret_cast<float4*>(sum + tc_ws_off(4 * c4, rr));
+          float4 acc = __ldcg(a0);
+#pragma unroll 8
+          for (int q = 1; q < splits; ++q) {
+            const float4 f =
+                __ldcg(reinterpret_cast<const float4*>(sum + size_t(q) * (kTcBM * BN) + tc_ws_off(4 * c4, rr)));
+            acc.x += f.x;
+            acc.y += f.y;
+            acc.z += f.z;
+            acc.w += f.w;
           }
+          __stcg(a0, acc);
+        }
+        named_sync(1, 32 * kTcEpiWarps);
+        if (row0 >= p.M) continue;
+        auto ld_sum = [&](int col, uint32_t* out) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) out[j] = __float_as_uint(a[j]);
+          for (int j = 0; j < 16; j += 4) {
+            const float4 f = row_ok ? __ldcg(reinterpret_cast<const float4*>(sum + tc_ws_off(col + j, r)))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            out[j] = __float_as_uint(f.x);
+            out[j + 1] = __float_as_uint(f.y);
+            out[j + 2] = __float_as_uint(f.z);
+            out[j + 3] = __float_as_uint(f.w);
+          }
         };
         tc_epilogue_tile<T, EPI, BN>(p, ld_sum, row0, tn * kUnitsPerTile, part, bufa, bufb, lane, out_seq);
       }

@@ -75,6 +75,7 @@ struct GemvParams {
   // push
   SeqRef out_seq;
   int out_chan;
+  int ts_cols;  // > 0: two-shot site, column u goes to rank ts_owner(u) only
   // argmax
   long long* best;
   uint32_t vocab_start;
@@ -174,8 +175,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int m, int u,
     const T val = from_f<T>(v0);
     const int par = out_seq & 1;
     const size_t off = size_t(m) * p.N + u;
-    for (int d = 0; d < p.comm.world; ++d) {
+    if (p.ts_cols > 0) {
+      const int d = ts_owner(u, p.ts_cols, p.comm.world);
       reinterpret_cast<T*>(p.comm.data(d, p.out_chan, par, p.comm.rank))[off] = val;
+    } else {
+      for (int d = 0; d < p.comm.world; ++d) {
+        reinterpret_cast<T*>(p.comm.data(d, p.out_chan, par, p.comm.rank))[off] = val;
+      }
     }
   } else if constexpr (EPI == kEpiArgmax) {
     const float v = round_t<T>(v0);

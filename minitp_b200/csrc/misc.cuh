@@ -2,6 +2,7 @@
 // and RMSNorm kernels.
 #pragma once
 
+#include "ar_rows.cuh"
 #include "comm.cuh"
 #include "ll.cuh"
 
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(256) ar_norm_kernel(const ArNormParams p) {
   const uint32_t seq = ld_volatile_u32(c.ctl() + kCtlColl) + 1u;
   const int par = seq & 1;
   const int r0 = blockIdx.x * p.rpc, r1 = min(p.rows, r0 + p.rpc);
-  const bool vec = (p.H % VE) == 0;
+  const bool vec = ar_rows_vec_ok<T>(p.H);
   if (c.world > 1) {
     const size_t e0 = size_t(r0) * p.H, e1 = size_t(r1) * p.H;
     const T* src = static_cast<const T*>(p.partial);
@@ -249,6 +250,14 @@ __global__ void __launch_bounds__(256) ar_norm_kernel(const ArNormParams p) {
     if (!wait_peers_cta(c, p.chan, seq, blockIdx.x)) return;
   }
   const T* gain = static_cast<const T*>(p.gain);
+  if (vec) {
+    for (int row = r0; row < r1; ++row)
+      ar_finish_row<T>(c, p.chan, par, 0, c.world > 1 ? nullptr : static_cast<const T*>(p.partial), row, p.H,
+                       static_cast<const T*>(p.bias), static_cast<const T*>(p.residual), static_cast<T*>(p.out_res),
+                       p.out_norm ? gain : nullptr, p.eps, static_cast<T*>(p.out_norm), red);
+    advance_counter(c, kCtlColl, kCtlCollDone, seq);
+    return;
+  }
   for (int row = r0; row < r1; ++row) {
     float ss = 0.f;
     for (int j = threadIdx.x; j < p.H; j += blockDim.x) {

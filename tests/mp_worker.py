@@ -88,7 +88,8 @@ def ctx_for(rank, world):
 # ---------------------------------------------------------------------- #
 # workers (module level: picklable under spawn)
 # ---------------------------------------------------------------------- #
-def w_generate(rank, world, name, dtype, n_layers_override=0):
+def w_generate(rank, world, name, dtype, n_layers_override=0, two_shot=False):
+    from minitp_b200 import _lib
     from minitp_b200 import config as mcfg
     from minitp_b200.generation import generate_greedy
     from minitp_b200.synthetic import make_prompt
@@ -100,6 +101,8 @@ def w_generate(rank, world, name, dtype, n_layers_override=0):
     cfg = fac()
     dt_ = torch.float32 if dtype == "fp32" else torch.bfloat16
     ctx = ctx_for(rank, world)
+    if two_shot:  # every AllReduce site that is not fused into a projection takes the two-shot form
+        _lib.call("mtpb_set_allreduce_two_shot", 0, 2)
     model = load_synthetic_tp(cfg, ctx, dtype=dt_, device=ctx.device)
     ids = make_prompt(cfg.vocab_size, b, p).cuda()
     logits = model(ids, positions=torch.arange(p, device="cuda"), gather_logits=True).float().cpu().numpy()
@@ -174,6 +177,33 @@ def w_collectives(rank, world):
     res["argmax_big"] = np.array([int(ops.argmax(c[:, s:e].contiguous().cuda(), s, comm)) for c in big_vocab_cases()])
     torch.cuda.synchronize()
     comm.raise_on_error()
+    return res
+
+
+def w_two_shot(rank, world, name):
+    """Prefill logits and greedy tokens of a model with its non-fused AllReduce sites one-shot, then
+    two-shot (reduce-scatter + all-gather): both forms sum in rank order with the same rounding."""
+    from minitp_b200 import _lib
+    from minitp_b200 import config as mcfg
+    from minitp_b200.generation import generate_greedy
+    from minitp_b200.synthetic import make_prompt
+    from minitp_b200.weight_loader import load_synthetic_tp
+
+    cfgs = {"q05b": (mcfg.qwen25_05b, 1, 128, 16), "q7b_l2": (lambda: mcfg.qwen25_7b(2), 2, 64, 8)}
+    fac, b, p, n = cfgs[name]
+    cfg = fac()
+    ctx = ctx_for(rank, world)
+    model = load_synthetic_tp(cfg, ctx, dtype=torch.bfloat16, device=ctx.device)
+    ids = make_prompt(cfg.vocab_size, b, p).cuda()
+    res = {}
+    for form, (min_bytes, min_world) in (("one", (-1, 2)), ("two", (0, 2))):
+        _lib.call("mtpb_set_allreduce_two_shot", min_bytes, min_world)
+        logits = model(ids, positions=torch.arange(p, device="cuda"), gather_logits=True)
+        res[f"{form}_logits"] = logits.view(torch.int16).cpu().numpy()
+        res[f"{form}_tokens"] = generate_greedy(model, ids, n, early_stop=False).cpu().numpy()
+    _lib.call("mtpb_set_allreduce_two_shot", 256 * 1024, 4)
+    torch.cuda.synchronize()
+    ctx.comm().raise_on_error()
     return res
 
 

@@ -85,6 +85,28 @@ def test_tp2_bf16_prefill_logits():
     assert np.array_equal(res[0]["tokens"], res[1]["tokens"])
 
 
+@pytest.mark.parametrize("world,name", [(2, "q05b"), (4, "q7b_l2")])
+def test_two_shot_sites_match_one_shot(world, name):
+    """The model's AllReduce sites outside the projections in the reduce-scatter + all-gather form:
+    prefill logits and greedy tokens bit-identical to the one-shot form, on every rank (bf16)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = mp_worker.run(world, mp_worker.w_two_shot, name)
+    for r in range(world):
+        assert np.array_equal(res[r]["one_logits"], res[r]["two_logits"]), r
+        assert np.array_equal(res[r]["one_tokens"], res[r]["two_tokens"]), r
+        assert np.array_equal(res[r]["two_tokens"], res[0]["two_tokens"]), r
+
+
+def test_tp2_fp32_tokens_two_shot_sites():
+    """The TP=2 model with every AllReduce site outside a projection in the two-shot form (prefill
+    sites and the final norm): tokens equal the reference's TP=2 run."""
+    res = mp_worker.run(2, mp_worker.w_generate, "q05b", "fp32", 0, True)
+    g = golden("model_q05b_tp2_fp32.npz")
+    for r in range(2):
+        assert np.array_equal(res[r]["tokens"], g["tokens"]), r
+
+
 def test_peer_timeout_is_reported():
     res = mp_worker.run(2, mp_worker.w_peer_timeout)
     assert bool(res[0]["ok_before"]) and bool(res[1]["ok_before"])
@@ -104,8 +126,9 @@ def test_tp4_padded_tokens_match_tp1():
 
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs >= 4 GPUs")
 def test_tp4_7b_tokens_match_reference_tp4():
-    """7B shape (2 layers, fp32) at TP=4: the reference's own TP=4 run (no padding, 1 KV head per rank)."""
-    res = mp_worker.run(4, mp_worker.w_generate, "q7b_l2", "fp32")
+    """7B shape (2 layers, fp32) at TP=4: the reference's own TP=4 run (no padding, 1 KV head per rank),
+    with the prefill's AllReduce sites in the two-shot form."""
+    res = mp_worker.run(4, mp_worker.w_generate, "q7b_l2", "fp32", 0, True)
     g = golden("model_q7b_l2_tp4_fp32.npz")
     g1 = golden("model_q7b_l2_tp1_fp32.npz")
     for r in range(4):
