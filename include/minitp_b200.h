@@ -64,8 +64,8 @@ int mtpb_set_tc_pair(int enable);
 
 /* Most K ranges per output tile of the single-CTA tensor-core GEMM (split K,
  * default 32; 1 turns it off); returns the previous value, -1 outside
- * [1, 64]. A projection whose output tiles fill at most half of the SMs
- * splits its K blocks into ranges (at least two 64-column blocks each, at
+ * [1, 64]. A projection of at most 64 rows whose output tiles fill at most
+ * half of the SMs splits its K blocks into ranges (at least two 64-column blocks each, at
  * most one item per SM); partials go to a per-device fp32 workspace (about
  * 64 KB per SM, allocated on the first split call, which must not be under
  * graph capture) and are summed in range order by the last arriving CTA, so
@@ -79,9 +79,10 @@ int mtpb_set_tc_split(int max_splits);
  * then all-gather (each rank reduces one column slice of every row and sends
  * the result to the others) for messages of at least min_bytes on at least
  * min_world ranks; smaller ones stay one-shot (every rank pushes its whole
- * partial to every peer). Defaults 262144 bytes and 4 ranks; min_bytes < 0
- * turns it off. Both forms sum in rank order with the same rounding, so
- * results are identical. The standalone mtpb_allreduce* calls stay one-shot.
+ * partial to every peer). min_bytes < 0 turns it off, which is the default
+ * (min_world 4): the extra flag round trip cost more than the copies saved
+ * on the 7B prefill at TP=4. Both forms sum in rank order with the same
+ * rounding, so results are identical. The standalone mtpb_allreduce* calls stay one-shot.
  * No counterpart in the reference (a tuning switch of this library). */
 int mtpb_set_allreduce_two_shot(long long min_bytes, int min_world);
 

@@ -331,11 +331,14 @@ TcPlan tc_plan(const GemvParams& p) {
   pl.tiles_m = (p.M + kTcBM - 1) / kTcBM;
   pl.bn = pl.tiles_m * tc_tiles_n<EPI>(p, 256) >= sms ? 256 : 128;
   pl.tiles_n = tc_tiles_n<EPI>(p, pl.bn);
-  // split K when the tiles fill at most half of the SMs: as many ranges as
-  // keep every item within one per SM, each of at least two K blocks
+  // split K for projections of at most 64 rows (decode steps of many rows)
+  // whose tiles fill at most half of the SMs: as many ranges as keep every
+  // item within one per SM, each of at least two K blocks. (On full 128-row
+  // tiles the last CTA's sum of the partials cost more than the split saved:
+  // a 128-token prefill of the 0.5B shape took 4.7 ms with it, 3.1 without.)
   const int tiles = pl.tiles_m * pl.tiles_n, nk = (p.K + kTcBK - 1) / kTcBK;
   pl.splits = 1;
-  if (pl.bn == 128 && g_tc_split_max > 1 && 2 * tiles <= sms)
+  if (pl.bn == 128 && g_tc_split_max > 1 && p.M <= 64 && 2 * tiles <= sms)
     pl.splits = std::max(1, std::min(std::min(sms / tiles, nk / 2), g_tc_split_max));
   pl.grid = std::min(tiles * pl.splits, sms);
   return pl;
@@ -535,8 +538,10 @@ int embed_run(int dtype, const EmbedParams& p, int grid, cudaStream_t st) {
 // Two-shot AllReduce sites of the model (reduce-scatter + all-gather,
 // comm.cuh) for messages of at least g_ts_min_bytes on at least
 // g_ts_min_world ranks: each rank then sends 2 (tp - 1) / tp of the message
-// instead of (tp - 1) copies, for one more flag round trip.
-long long g_ts_min_bytes = 256 * 1024;
+// instead of (tp - 1) copies, for one more flag round trip. Off by default:
+// on the 7B shape at TP=4 a 1024-token prefill took 7.05 ms with every such
+// site two-shot and 6.87 ms one-shot (8 layers; 46.3 vs 45.4 ms at batch 8).
+long long g_ts_min_bytes = -1;
 int g_ts_min_world = 4;
 
 // Column slice width of a two-shot site of rows of H values (0: one-shot).

@@ -201,7 +201,7 @@ def w_two_shot(rank, world, name):
         logits = model(ids, positions=torch.arange(p, device="cuda"), gather_logits=True)
         res[f"{form}_logits"] = logits.view(torch.int16).cpu().numpy()
         res[f"{form}_tokens"] = generate_greedy(model, ids, n, early_stop=False).cpu().numpy()
-    _lib.call("mtpb_set_allreduce_two_shot", 256 * 1024, 4)
+    _lib.call("mtpb_set_allreduce_two_shot", -1, 4)
     torch.cuda.synchronize()
     ctx.comm().raise_on_error()
     return res
