@@ -36,6 +36,7 @@ struct AttnParams {
 
 constexpr int kAttnThreads = 128;
 constexpr int kAttnGB = 4;  // heads per PV pass
+constexpr int kAttnU = 4;   // K / V rows (and merged splits) whose loads are issued together
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) {
@@ -77,22 +78,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qf[i] = to_f(qrow[i]);
   __syncthreads();
 
-  // scores: LPP lanes per key row, PPW rows per warp pass
+  // scores: LPP lanes per key row, PPW rows per warp pass; the K rows of
+  // kAttnU passes are loaded before any of them is used
   {
     const int pg = lane / LPP, li = lane - pg * LPP;
-    for (int r0 = s0 + warp * PPW; r0 < s1; r0 += NW * PPW) {
-      const int r = r0 + pg;
-      const bool ok = r < s1;
-      float kf[VE];
-      unpack(ok ? ld_vec(kbase + size_t(r) * HD + li * VE) : make_uint4(0, 0, 0, 0), kf);
-      for (int g = 0; g < G; ++g) {
-        const float* qg = qf + g * HD + li * VE;
-        float d = 0.f;
+    for (int rb = s0 + warp * PPW; rb < s1; rb += NW * PPW * kAttnU) {
+      uint4 kv[kAttnU];
 #pragma unroll
-        for (int e = 0; e < VE; ++e) d = fmaf(kf[e], qg[e], d);
+      for (int u = 0; u < kAttnU; ++u) {
+        const int r = rb + u * NW * PPW + pg;
+        kv[u] = r < s1 ? ld_vec(kbase + size_t(r) * HD + li * VE) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-        for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (ok && li == 0) sc[g * p.chunk_cap + (r - s0)] = d * p.scale;
+      for (int u = 0; u < kAttnU; ++u) {
+        const int r = rb + u * NW * PPW + pg;
+        const bool ok = r < s1;
+        float kf[VE];
+        unpack(kv[u], kf);
+        for (int g = 0; g < G; ++g) {
+          const float* qg = qf + g * HD + li * VE;
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < VE; ++e) d = fmaf(kf[e], qg[e], d);
+#pragma unroll
+          for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          if (ok && li == 0) sc[g * p.chunk_cap + (r - s0)] = d * p.scale;
+        }
       }
     }
   }
@@ -128,15 +139,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
     for (int gg = 0; gg < kAttnGB; ++gg)
 #pragma unroll
       for (int e = 0; e < VE; ++e) acc[gg][e] = 0.f;
-    for (int r = pl; r < n; r += NPL) {
-      float vf[VE];
-      unpack(ld_vec(vbase + size_t(s0 + r) * HD + dc * VE), vf);
+    for (int rb = pl; rb < n; rb += NPL * kAttnU) {
+      uint4 vv[kAttnU];
 #pragma unroll
-      for (int gg = 0; gg < kAttnGB; ++gg) {
-        if (g0 + gg < G) {
-          const float pr = sc[(g0 + gg) * p.chunk_cap + r];
+      for (int u = 0; u < kAttnU; ++u) {
+        const int r = rb + u * NPL;
+        vv[u] = r < n ? ld_vec(vbase + size_t(s0 + r) * HD + dc * VE) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int e = 0; e < VE; ++e) acc[gg][e] = fmaf(pr, vf[e], acc[gg][e]);
+      for (int u = 0; u < kAttnU; ++u) {
+        const int r = rb + u * NPL;
+        if (r < n) {
+          float vf[VE];
+          unpack(vv[u], vf);
+#pragma unroll
+          for (int gg = 0; gg < kAttnGB; ++gg) {
+            if (g0 + gg < G) {
+              const float pr = sc[(g0 + gg) * p.chunk_cap + r];
+#pragma unroll
+              for (int e = 0; e < VE; ++e) acc[gg][e] = fmaf(pr, vf[e], acc[gg][e]);
+            }
+          }
         }
       }
     }
@@ -187,15 +210,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
     const int head = kvh * G + g;
     const float* mlh = p.part_ml + (size_t(m) * p.hq + head) * p.nsplit * 2;
     const float* oh = p.part_o + (size_t(m) * p.hq + head) * p.nsplit * HD;
+    // kAttnU splits' values are loaded before they are combined (in split order)
     float mx = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) mx = fmaxf(mx, __ldcg(mlh + 2 * s));
+    for (int sb = 0; sb < p.nsplit; sb += kAttnU) {
+      float t[kAttnU];
+#pragma unroll
+      for (int u = 0; u < kAttnU; ++u) t[u] = sb + u < p.nsplit ? __ldcg(mlh + 2 * (sb + u)) : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kAttnU; ++u) mx = fmaxf(mx, t[u]);
+    }
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < p.nsplit; ++s) {
-      const float ms = __ldcg(mlh + 2 * s);
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - mx);
-      num = fmaf(w, __ldcg(oh + size_t(s) * HD + d), num);
-      den = fmaf(w, __ldcg(mlh + 2 * s + 1), den);
+    for (int sb = 0; sb < p.nsplit; sb += kAttnU) {
+      float ms[kAttnU], ls[kAttnU], os[kAttnU];
+#pragma unroll
+      for (int u = 0; u < kAttnU; ++u) {
+        const bool in = sb + u < p.nsplit;
+        ms[u] = in ? __ldcg(mlh + 2 * (sb + u)) : -INFINITY;
+        ls[u] = in ? __ldcg(mlh + 2 * (sb + u) + 1) : 0.f;
+        os[u] = in ? __ldcg(oh + size_t(sb + u) * HD + d) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kAttnU; ++u) {
+        if (ms[u] == -INFINITY) continue;
+        const float w = expf(ms[u] - mx);
+        num = fmaf(w, os[u], num);
+        den = fmaf(w, ls[u], den);
+      }
     }
     static_cast<T*>(p.out)[size_t(m) * p.hq * HD + size_t(head) * HD + d] = from_f<T>(num / den);
   }
