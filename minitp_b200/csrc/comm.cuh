@@ -126,9 +126,10 @@ __device__ __forceinline__ bool wait_peers(const Comm& c, int chan, uint32_t seq
   __shared__ int s_ok;
   if (threadIdx.x < 32) {
     const int par = seq & 1;
-    bool ok = true;
-    for (int src = 0; src < c.world && ok; ++src)
-      ok = warp_poll_flags(c.flag(c.rank, chan, par, src, 0), nprod, seq, true, c.status(), c.timeout_ns);
+    // every rank's producer flags in one poll (consecutive ranks' flags are
+    // kMaxCtas apart)
+    const bool ok = warp_poll_flags(c.flag(c.rank, chan, par, 0, 0), nprod, seq, true, c.status(), c.timeout_ns,
+                                    nullptr, c.world, size_t(kMaxCtas));
     if (threadIdx.x == 0) {
       s_ok = ok ? 1 : 0;
       if (!ok) atomicOr(c.status(), kStatusTimeout);
@@ -147,9 +148,8 @@ __device__ __forceinline__ bool wait_peers_cta(const Comm& c, int chan, uint32_t
   __shared__ int s_ok2;
   if (threadIdx.x < 32) {
     const int par = seq & 1;
-    bool ok = true;
-    for (int src = 0; src < c.world && ok; ++src)
-      ok = warp_poll_flags(c.flag(c.rank, chan, par, src, cta), 1, seq, true, c.status(), c.timeout_ns);
+    const bool ok = warp_poll_flags(c.flag(c.rank, chan, par, 0, cta), 1, seq, true, c.status(), c.timeout_ns,
+                                    nullptr, c.world, size_t(kMaxCtas));
     if (threadIdx.x == 0) {
       s_ok2 = ok ? 1 : 0;
       if (!ok) atomicOr(c.status(), kStatusTimeout);

@@ -149,34 +149,39 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
   return v;
 }
 
-// One warp polls flags[0, n) until every flag reached `seq` (wrap-safe),
-// with 16-byte loads when `flags` is 16-byte aligned and a short sleep
-// between rounds so that many CTAs polling at once do not flood L2. After
-// success an acquire fence at `sys` (else gpu) scope orders the caller's
-// later reads after the producers' releases. Bounded: returns false when
-// `timeout_ns` passed, *status became non-zero or *abort became non-zero.
-// All lanes of the warp must call it; all return the same value.
+// One warp polls flags[s * src_stride + i] for sources s < nsrc and i < n
+// until every flag reached `seq` (wrap-safe); each round issues the loads of
+// every source before it tests any (16-byte loads when the flags are 16-byte
+// aligned), with a short sleep between rounds so that many CTAs polling at
+// once do not flood L2. After success an acquire fence at `sys` (else gpu)
+// scope orders the caller's later reads after the producers' releases.
+// Bounded: returns false when `timeout_ns` passed, *status became non-zero or
+// *abort became non-zero. All lanes of the warp must call it; all return the
+// same value.
 __device__ __forceinline__ bool warp_poll_flags(const uint32_t* flags, int n, uint32_t seq, bool sys,
                                                 uint32_t* status, uint64_t timeout_ns,
-                                                const volatile int* abort = nullptr) {
+                                                const volatile int* abort = nullptr, int nsrc = 1,
+                                                size_t src_stride = 0) {
   const int lane = threadIdx.x & 31;
-  const bool vec = (reinterpret_cast<uintptr_t>(flags) & 15u) == 0;
+  const bool vec = (reinterpret_cast<uintptr_t>(flags) & 15u) == 0 && (src_stride & 3u) == 0;
   uint64_t t0 = 0;
   uint32_t round = 0;
   while (true) {
     bool mine = true;
-    if (vec) {
-      for (int i = lane * 4; i < n; i += 128) {
-        if (i + 3 < n) {
-          const uint4 v = ld_volatile_v4(flags + i);
-          mine = mine && seq_reached(v.x, seq) && seq_reached(v.y, seq) && seq_reached(v.z, seq) &&
-                 seq_reached(v.w, seq);
-        } else {
-          for (int j = i; j < n; ++j) mine = mine && seq_reached(ld_volatile_u32(flags + j), seq);
+    for (int sidx = 0; sidx < nsrc; ++sidx) {
+      const uint32_t* f = flags + size_t(sidx) * src_stride;
+      if (vec) {
+        for (int i = lane * 4; i < n; i += 128) {
+          if (i + 3 < n) {
+            const uint4 v = ld_volatile_v4(f + i);
+            mine &= seq_reached(v.x, seq) & seq_reached(v.y, seq) & seq_reached(v.z, seq) & seq_reached(v.w, seq);
+          } else {
+            for (int j = i; j < n; ++j) mine &= seq_reached(ld_volatile_u32(f + j), seq);
+          }
         }
+      } else {
+        for (int i = lane; i < n; i += 32) mine &= seq_reached(ld_volatile_u32(f + i), seq);
       }
-    } else {
-      for (int i = lane; i < n; i += 32) mine = mine && seq_reached(ld_volatile_u32(flags + i), seq);
     }
     if (__all_sync(0xffffffffu, mine)) break;
     ++round;
