@@ -1,4 +1,5 @@
-// Tensor-core GEMM for the prefill projections (bf16): y = x · Wᵀ with the
+// Tensor-core GEMM for the bf16 projections of many rows (prefill chunks of
+// >= 64 rows, kernel-chain decode steps of >= 8 rows): y = x · Wᵀ with the
 // GEMV path's epilogues (store, SwiGLU, RoPE + KV append, AllReduce push).
 //
 // Persistent kernel, one CTA per SM, each CTA walking output tiles of

@@ -54,3 +54,24 @@ def test_cpu_tensors_raise_no_fallback(lib):
 
     with pytest.raises(_lib.MinitpB200Error, match="CUDA"):
         ops.linear(torch.zeros(1, 16), torch.zeros(8, 16))
+
+
+def test_two_shot_slice_rule(lib):
+    """Which AllReduce form a model site gets: one-shot by default; with the switch on, the two-shot
+    column slice of ceil(H / tp) rounded up to whole 16-byte vectors, only from the set size and
+    rank count on (host logic; no GPU needed)."""
+    bf16 = _lib.MTPB_BF16
+    assert lib.mtpb_allreduce_two_shot_cols(1 << 24, 3584, 8, bf16) == 0  # off by default
+    try:
+        assert lib.mtpb_set_allreduce_two_shot(1 << 20, 4) == 0
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 3584, 8, bf16) == 448
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 896, 4, bf16) == 224
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 896, 8, _lib.MTPB_F32) == 112
+        assert lib.mtpb_allreduce_two_shot_cols((1 << 20) - 1, 3584, 8, bf16) == 0  # below the size
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 3584, 2, bf16) == 0  # below the rank count
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 900, 4, bf16) == 0  # rows of partial vectors
+        assert lib.mtpb_set_allreduce_two_shot(1 << 20, 2) == 0
+        assert lib.mtpb_allreduce_two_shot_cols(1 << 20, 896, 3, bf16) == 304  # 298.7 -> 38 vectors of 8
+        assert lib.mtpb_set_allreduce_two_shot(0, 1) == _lib.ERR_INVALID
+    finally:
+        lib.mtpb_set_allreduce_two_shot(-1, 4)
