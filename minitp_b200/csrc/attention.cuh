@@ -241,4 +241,195 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill form (tokens per batch row >= kAttnPfMinT, head dim 64 or 128): a
+// CTA takes a tile of consecutive query tokens of one batch row and all G
+// query heads of one KV head (R = QT * G rows, R <= 16 * RPT), and streams
+// the keys [0, last position of the tile] through shared memory in tiles of
+// 64 rows, so each K/V row is read once per query tile instead of once per
+// query. Scores and P.V run on the CUDA cores from shared memory with an
+// online softmax (running max and sum per row, rescaled per key tile):
+//   scores  thread (rg = tid / 16, kg = tid % 16): rows rg*RPT.., keys kg + 16 k
+//   P.V     thread (rg, dg = tid % 16): rows rg*RPT.., dims dg*HD/16..
+// The 16 threads of a row group are one half-warp, so a row's tile max and
+// sum are half-warp shuffles and its rescale factor is in every thread that
+// holds that row's output. Causal rule as above (key j <= position of the
+// query); rows past the batch row's tokens compute on zeros and write nothing.
+// ---------------------------------------------------------------------------
+constexpr int kAttnPfThreads = 256;
+constexpr int kAttnPfKT = 64;    // keys per tile
+constexpr int kAttnPfMinT = 16;  // tokens per batch row from which prefill uses this form
+constexpr int kAttnPfPad = 4;    // row padding of the shared-memory tiles (floats)
+
+template <int HD, int RPT>
+__host__ __device__ constexpr size_t attn_pf_smem() {
+  return (size_t(16 * RPT) * (HD + kAttnPfPad) + 2 * size_t(kAttnPfKT) * (HD + kAttnPfPad) +
+          size_t(16 * RPT) * (kAttnPfKT + kAttnPfPad)) *
+         sizeof(float);
+}
+
+template <typename T, int HD, int RPT>
+__global__ void __launch_bounds__(kAttnPfThreads, 1) attn_prefill_kernel(const AttnParams p) {
+  constexpr int VE = VecTraits<T>::kElems;
+  constexpr int R = 16 * RPT;   // rows (query, head) per CTA at most
+  constexpr int DPT = HD / 16;  // output dims per thread
+  constexpr int QS = HD + kAttnPfPad, KS = HD + kAttnPfPad, PS = kAttnPfKT + kAttnPfPad;
+  extern __shared__ __align__(16) float smf[];
+  float* qs = smf;                          // [R][QS]
+  float* ks = qs + size_t(R) * QS;          // [KT][KS]
+  float* vs = ks + size_t(kAttnPfKT) * KS;  // [KT][KS]
+  float* ps = vs + size_t(kAttnPfKT) * KS;  // [R][PS]
+
+  pdl_launch();
+  pdl_wait();
+  const int G = p.hq / p.hkv;
+  const int QT = R / G;  // query tokens per CTA
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int t0 = blockIdx.x * QT;
+  const int T_ = p.tpr;
+  if (t0 >= T_) return;
+  const int nq = min(QT, T_ - t0);  // valid query tokens of this tile
+  const int pos0 = (p.pos_ptr ? *p.pos_ptr : p.pos_base) + t0;
+  const int kend = pos0 + nq;  // keys [0, kend)
+  if (pos0 < 0 || kend > p.cap) {
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusBadPosition);
+    return;
+  }
+  const int tid = threadIdx.x, rg = tid >> 4, sub = tid & 15;
+  const T* kbase = static_cast<const T*>(p.k_cache) + (size_t(b) * p.hkv + kvh) * p.cap * HD;
+  const T* vbase = static_cast<const T*>(p.v_cache) + (size_t(b) * p.hkv + kvh) * p.cap * HD;
+
+  // q rows: row r = qi * G + g (zeros past the valid rows)
+  for (int i = tid; i < R * (HD / VE); i += kAttnPfThreads) {
+    const int r = i / (HD / VE), c = i - r * (HD / VE);
+    const int qi = r / G, g = r - qi * G;
+    float f[VE];
+    if (qi < nq) {
+      const size_t m = size_t(b) * T_ + t0 + qi;
+      unpack(ld_vec(static_cast<const T*>(p.q) + m * p.hq * HD + size_t(kvh * G + g) * HD + c * VE), f);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VE; ++e) f[e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < VE; ++e) qs[size_t(r) * QS + c * VE + e] = f[e];
+  }
+  // the last key position each of this thread's rows may see (rows past the
+  // valid queries see every key of the range: finite scores, no output)
+  int lim[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg * RPT + i, qi = r / G;
+    lim[i] = qi < nq ? pos0 + qi : kend - 1;
+  }
+  float mrow[RPT], lrow[RPT], o[RPT][DPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPT; ++d) o[i][d] = 0.f;
+  }
+
+  for (int j0 = 0; j0 < kend; j0 += kAttnPfKT) {
+    __syncthreads();  // the previous tile's K/V/P are consumed (and q is staged)
+    for (int i = tid; i < kAttnPfKT * (HD / VE); i += kAttnPfThreads) {
+      const int j = i / (HD / VE), c = i - j * (HD / VE);
+      float kf[VE], vf[VE];
+      if (j0 + j < kend) {
+        unpack(ld_vec(kbase + size_t(j0 + j) * HD + c * VE), kf);
+        unpack(ld_vec(vbase + size_t(j0 + j) * HD + c * VE), vf);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VE; ++e) kf[e] = vf[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        ks[size_t(j) * KS + c * VE + e] = kf[e];
+        vs[size_t(j) * KS + c * VE + e] = vf[e];
+      }
+    }
+    __syncthreads();
+    // scores of rows rg*RPT.. against keys sub + 16 k (consecutive threads on
+    // consecutive K rows: conflict-free 16-byte loads)
+    float sc[RPT][4];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sc[i][k] = 0.f;
+    for (int d = 0; d < HD; d += 4) {
+      float4 kv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kv[k] = *reinterpret_cast<const float4*>(ks + size_t(sub + 16 * k) * KS + d);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float4 qv = *reinterpret_cast<const float4*>(qs + size_t(rg * RPT + i) * QS + d);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          sc[i][k] = fmaf(qv.w, kv[k].w, fmaf(qv.z, kv[k].z, fmaf(qv.y, kv[k].y, fmaf(qv.x, kv[k].x, sc[i][k]))));
+      }
+    }
+    // online softmax: tile max and sum per row over the half-warp
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      float tm = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int j = j0 + sub + 16 * k;
+        sc[i][k] = j <= lim[i] ? sc[i][k] * p.scale : -INFINITY;
+        tm = fmaxf(tm, sc[i][k]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+      const float mn = fmaxf(mrow[i], tm);  // finite: key 0 is in the first tile of every row
+      const float alpha = expf(mrow[i] - mn);
+      float ts = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float e = expf(sc[i][k] - mn);
+        ps[size_t(rg * RPT + i) * PS + sub + 16 * k] = e;
+        ts += e;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) ts += __shfl_xor_sync(0xffffffffu, ts, off);
+      lrow[i] = lrow[i] * alpha + ts;
+      mrow[i] = mn;
+#pragma unroll
+      for (int d = 0; d < DPT; ++d) o[i][d] *= alpha;
+    }
+    __syncwarp();  // a row group's P entries come from the same half-warp
+    // P.V: rows rg*RPT.., dims sub*DPT..
+    const int kn = min(kAttnPfKT, kend - j0);
+    for (int j = 0; j < kn; ++j) {
+      float vv[DPT];
+#pragma unroll
+      for (int d = 0; d < DPT; d += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vs + size_t(j) * KS + sub * DPT + d);
+        vv[d] = v4.x;
+        vv[d + 1] = v4.y;
+        vv[d + 2] = v4.z;
+        vv[d + 3] = v4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const float pr = ps[size_t(rg * RPT + i) * PS + j];
+#pragma unroll
+        for (int d = 0; d < DPT; ++d) o[i][d] = fmaf(pr, vv[d], o[i][d]);
+      }
+    }
+  }
+  // normalise and store the valid rows
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg * RPT + i, qi = r / G, g = r - qi * G;
+    if (qi < nq) {
+      const size_t m = size_t(b) * T_ + t0 + qi;
+      T* dst = static_cast<T*>(p.out) + m * p.hq * HD + size_t(kvh * G + g) * HD + sub * DPT;
+      const float inv = 1.0f / lrow[i];
+#pragma unroll
+      for (int d = 0; d < DPT; ++d) dst[d] = from_f<T>(o[i][d] * inv);
+    }
+  }
+}
+
 }  // namespace mtpb

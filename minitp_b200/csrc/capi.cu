@@ -464,6 +464,18 @@ int attn_launch_t(AttnParams p, int hd, cudaStream_t st) {
   }
 }
 
+template <typename T>
+int attn_pf_launch(const AttnParams& p, int hd, int G, int rpt, cudaStream_t st) {
+  const int qt = 16 * rpt / G;
+  dim3 grid((p.tpr + qt - 1) / qt, p.hkv, p.M / p.tpr);
+  if (hd == 64 && rpt == 8)
+    return launch(attn_prefill_kernel<T, 64, 8>, grid, dim3(kAttnPfThreads), attn_pf_smem<64, 8>(), st, p);
+  if (hd == 64) return launch(attn_prefill_kernel<T, 64, 4>, grid, dim3(kAttnPfThreads), attn_pf_smem<64, 4>(), st, p);
+  if (rpt == 8)
+    return launch(attn_prefill_kernel<T, 128, 8>, grid, dim3(kAttnPfThreads), attn_pf_smem<128, 8>(), st, p);
+  return launch(attn_prefill_kernel<T, 128, 4>, grid, dim3(kAttnPfThreads), attn_pf_smem<128, 4>(), st, p);
+}
+
 int attn_run(int dtype, const void* q, const void* kc, const void* vc, void* out, int B, int T, int hq,
              int hkv, int hd, int cap, const int* pos_ptr, int pos_base, AttnScratch& scr,
              uint32_t* status, cudaStream_t st) {
@@ -487,6 +499,15 @@ int attn_run(int dtype, const void* q, const void* kc, const void* vc, void* out
   p.pos_ptr = pos_ptr;
   p.pos_base = pos_base;
   p.scale = 1.0f / std::sqrt(float(hd));
+  // prefill: query tiles with K/V streamed through shared memory (no scratch)
+  if (T >= kAttnPfMinT && (hd == 64 || hd == 128)) {
+    p.nsplit = 1;
+    // 128 (query, head) rows per CTA when that still gives every SM a tile, else 64
+    const bool big = (T + 128 / G - 1) / (128 / G) * hkv * B >= sm_count();
+    if (dtype == MTPB_BF16) return attn_pf_launch<bf16>(p, hd, G, big ? 8 : 4, st);
+    if (dtype == MTPB_F32) return attn_pf_launch<float>(p, hd, G, big ? 8 : 4, st);
+    return fail(MTPB_ERR_INVALID, "unsupported dtype");
+  }
   p.nsplit = attn_choose_splits(M, hkv, G, cap, hd, &p.chunk_cap);
   p.status = status;
   if (p.nsplit > 1) {

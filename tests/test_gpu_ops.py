@@ -76,7 +76,8 @@ def test_rmsnorm(lib, dtype, H):
 
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
 @pytest.mark.parametrize("hq,hkv,hd", [(7, 1, 64), (14, 2, 64), (4, 2, 16), (7, 1, 128), (4, 1, 128)])
-@pytest.mark.parametrize("T,cache_len", [(1, 0), (1, 37), (1, 300), (9, 0), (5, 11)])
+@pytest.mark.parametrize("T,cache_len", [(1, 0), (1, 37), (1, 300), (9, 0), (5, 11), (16, 0), (100, 0), (257, 20),
+                                         (40, 130)])
 def test_qkv_rope_attention(lib, dtype, hq, hkv, hd, T, cache_len):
     """Fused QKV + RoPE + KV append, then split-KV GQA attention, vs the oracle."""
     from minitp_b200 import ops
