@@ -255,8 +255,8 @@ def kv_bytes_per_token(model, batch: int, avg_len: float) -> float:
 # (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (model, batch, TP,
 # kernel revision). Configurations without a capture of the current kernel
 # report null.
-MK_TRAFFIC: dict = {("qwen2.5-0.5b", 1, 1, 2): 994_579_200}
-MK_REVISION = 2
+MK_TRAFFIC: dict = {("qwen2.5-0.5b", 1, 1, 2): 994_579_200, ("qwen2.5-0.5b", 1, 1, 3): 994_149_376}
+MK_REVISION = 3
 
 
 def measured_traffic(model_name: str, batch: int, world: int, step_launches: int):
